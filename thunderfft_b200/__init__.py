@@ -1,0 +1,194 @@
+"""thunderfft_b200 — B200-native (sm_100a) tensor-core batched FFT.
+
+Python mirror of the ThunderFFT host API over the C ABI of
+``libthunderfft_b200.so`` (include/thff.h).  The names follow the reference's
+header API (include/thunderfft/thunderfft.cuh):
+
+=====================================  =======================================
+reference (C++ templates)              here
+=====================================  =======================================
+``ThunderFFTInitialize<T>(N)``         ``ThunderFFTInitialize(T, N)``
+``ThunderFFTFinalize<T>()``            ``ThunderFFTFinalize(T)``
+``ThunderFFT_global<T,N,fwd>(i,o,b,s)`` ``ThunderFFT_global(T, N, fwd, i, o, b, s)``
+=====================================  =======================================
+
+``T`` is ``"float"`` (float2 storage, TF32 tensor-core arithmetic) or
+``"half"`` (half2 storage, FP16 tensor-core arithmetic).  Argument errors raise
+``ValueError`` (the reference's ``std::invalid_argument``); CUDA failures and
+device-side timeouts raise ``RuntimeError`` (``std::runtime_error``).
+
+There is no CPU fallback: every entry point needs the compiled library and a
+B200; a missing ``.so`` raises at first use.
+
+Convenience wrappers on torch tensors (``fft``, ``ifft``) are provided for
+tests and benchmarks; torch is only used for device memory and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional
+
+__all__ = [
+    "ThunderFFTInitialize", "ThunderFFTFinalize", "ThunderFFT_global", "c2c_async", "sync_check",
+    "twiddle_table", "fft", "load_library", "library_path", "SUPPORTED_N", "batch_per_block",
+    "warp_per_block", "threads_per_warp", "version",
+]
+
+SUPPORTED_N = (64, 128, 256, 512, 1024, 2048, 4096)
+# Launch tuples of the reference header (detail/thunderfft_impl.cuh:14-32);
+# kept for API compatibility of the device-side composition helpers.
+batch_per_block = {64: 16, 128: 8, 256: 16, 512: 2, 1024: 1, 2048: 1, 4096: 1}
+warp_per_block = {64: 1, 128: 1, 256: 4, 512: 1, 1024: 1, 2048: 2, 4096: 4}
+threads_per_warp = 32
+
+THFF_OK, THFF_INVALID_ARGUMENT, THFF_CUDA_ERROR, THFF_DEVICE_TIMEOUT, THFF_UNSUPPORTED = range(5)
+_DTYPES = {"float": 0, "half": 1, "f32": 0, "f16": 1, "tf32": 0, "fp16": 1}
+
+_PKG = Path(__file__).resolve().parent
+_lib: Optional[ctypes.CDLL] = None
+
+
+def library_path() -> Path:
+    return Path(os.environ.get("THFF_LIBRARY", _PKG / "libthunderfft_b200.so"))
+
+
+def load_library() -> ctypes.CDLL:
+    """Load the compiled backend; raise if it is missing (no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = library_path()
+    if not path.exists():
+        raise RuntimeError(
+            f"[ThunderFFT] {path} is missing: build it with `python -m thunderfft_b200.build` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(path))
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+    lib.thff_version.restype = ctypes.c_char_p
+    lib.thff_last_error.restype = ctypes.c_char_p
+    lib.thff_initialize.argtypes = [i32, i32]
+    lib.thff_finalize.argtypes = [i32]
+    lib.thff_twiddle_table.argtypes = [i32, ctypes.POINTER(vp), ctypes.POINTER(i32)]
+    lib.thff_global.argtypes = [i32, i32, i32, vp, vp, i32, vp]
+    lib.thff_c2c_async.argtypes = [i32, i32, i32, vp, vp, i64, vp]
+    lib.thff_sync_check.argtypes = [vp]
+    for name in ("thff_initialize", "thff_finalize", "thff_twiddle_table", "thff_global",
+                 "thff_c2c_async", "thff_sync_check"):
+        getattr(lib, name).restype = i32
+    _lib = lib
+    return lib
+
+
+def _dtype_code(T) -> int:
+    key = T if isinstance(T, str) else getattr(T, "__name__", str(T))
+    try:
+        return _DTYPES[key]
+    except KeyError:
+        raise ValueError(f"ThunderFFT supports float and half only (got {T!r})") from None
+
+
+def _check(status: int) -> None:
+    if status == THFF_OK:
+        return
+    msg = load_library().thff_last_error().decode(errors="replace")
+    if status == THFF_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def version() -> str:
+    return load_library().thff_version().decode()
+
+
+def ThunderFFTInitialize(T, N: int) -> None:
+    """Prepare twiddles/constants for length N on the current device
+    (reference: ThunderFFTInitialize<T>(N), thunderfft_impl_twiddle.cuh:279-327)."""
+    code = _dtype_code(T)
+    if N not in SUPPORTED_N:  # before any CUDA call, like the reference
+        raise ValueError("ThunderFFTInitialize<T>: unsupported FFT size")
+    _check(load_library().thff_initialize(code, int(N)))
+
+
+def ThunderFFTFinalize(T) -> None:
+    """Release the current device's cached table (reference: ThunderFFTFinalize<T>())."""
+    _check(load_library().thff_finalize(_dtype_code(T)))
+
+
+def twiddle_table(T):
+    """(device pointer, N) of the current device's cached twiddle table."""
+    p, n = ctypes.c_void_p(), ctypes.c_int()
+    _check(load_library().thff_twiddle_table(_dtype_code(T), ctypes.byref(p), ctypes.byref(n)))
+    return (p.value or 0), n.value
+
+
+def _ptr(x) -> int:
+    if x is None:
+        return 0
+    if isinstance(x, int):
+        return x
+    return int(x.data_ptr())
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        return 0
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+def ThunderFFT_global(T, N: int, forward: bool, d_input, d_output, batch: int, stream=None) -> None:
+    """Batched C2C FFT with the reference wrapper's contract
+    (ThunderFFT_global<T,N,forward>, thunderfft_impl_kernel.cuh:6-41):
+    batch < 0 -> ValueError; batch == 0 -> no-op before any CUDA or pointer
+    access; null/identical pointers -> ValueError; synchronizes ``stream``.
+    ``d_input``/``d_output`` are device pointers (int) or CUDA tensors."""
+    code = _dtype_code(T)
+    if N not in SUPPORTED_N:
+        raise ValueError("Unsupported ThunderFFT length")
+    if batch < 0:
+        raise ValueError("ThunderFFT batch must be nonnegative")
+    if batch == 0:
+        return
+    _check(load_library().thff_global(code, int(N), 1 if forward else 0, _ptr(d_input), _ptr(d_output),
+                                      int(batch), _stream_handle(stream)))
+
+
+def c2c_async(T, N: int, forward: bool, d_input, d_output, batch: int, stream=None) -> None:
+    """Asynchronous form (64-bit batch; no stream synchronization)."""
+    _check(load_library().thff_c2c_async(_dtype_code(T), int(N), 1 if forward else 0, _ptr(d_input),
+                                         _ptr(d_output), int(batch), _stream_handle(stream)))
+
+
+def sync_check(stream=None) -> None:
+    """Synchronize ``stream`` and raise if a kernel recorded a device-side timeout."""
+    _check(load_library().thff_sync_check(_stream_handle(stream)))
+
+
+def fft(x, forward: bool = True, out=None, stream=None, sync: bool = True):
+    """Transform the last axis of a CUDA tensor.
+
+    ``x``: complex64 (float path) or float16 with a trailing axis of 2
+    (re, im) (half path); last complex length in SUPPORTED_N; contiguous.
+    Returns ``out`` (allocated like ``x`` when None)."""
+    import torch
+
+    if not x.is_cuda:
+        raise ValueError("ThunderFFT operates on CUDA tensors only")
+    if x.dtype == torch.complex64:
+        T, n = "float", x.shape[-1]
+    elif x.dtype == torch.float16 and x.shape[-1] == 2:
+        T, n = "half", x.shape[-2]
+    else:
+        raise ValueError("expected complex64, or float16 with a trailing (re, im) axis")
+    if not x.is_contiguous():
+        raise ValueError("input must be contiguous")
+    batch = x.numel() // (n if T == "float" else 2 * n)
+    if out is None:
+        out = torch.empty_like(x)
+    c2c_async(T, n, forward, x, out, batch, stream if stream is not None else torch.cuda.current_stream())
+    if sync:
+        sync_check(stream if stream is not None else torch.cuda.current_stream())
+    return out

@@ -1,0 +1,642 @@
+// fft_kernels.cuh — batched C2C FFT kernels for sm_100a (tcgen05 + TMA).
+//
+// Two kernel families compute the same transform as the reference's
+// ThunderFFT_global_kernel (include/thunderfft/detail/kernel/global_kernel.cuh:21-100):
+//
+//  * fft2_kernel  — N = Ns * Na in two tensor-core stages.
+//      x[n], n = a + Na*s  (a: contiguous index, s: strided index).
+//      stage 1 (DFT over s, length Ns):  Y[a][ks] = sum_s x[a + Na s] w_Ns^(s ks)
+//      twiddle:                         Y'[a][ks] = Y[a][ks] * w_N^(a ks)
+//      stage 2 (DFT over a, length Na):  X[Ns ka + ks] = sum_a Y'[a][ks] w_Na^(a ka)
+//    Each stage is one UMMA D = A x B with
+//      A = the real-valued stage DFT matrix, rows (ks, re|im) in 16-row blocks
+//          [8 rows cos | 8 rows sin], columns = the stage's input index,
+//          K-major, no swizzle, resident in shared memory for the whole kernel;
+//          G independent signal groups share one MMA through a block-diagonal
+//          A (K = G*L rows of B, M = 2*G*L rows of A);
+//      B = the data, MN-major: K rows = stage input index, N columns =
+//          (signal, other index, re|im).  Stage-1 B is the natural input
+//          layout brought in by one TMA box per tile; stage-2 B is written by
+//          the stage-1 epilogue.
+//    A 16x256b TMEM load then hands each thread, for one (ks, a) pair, the
+//    four partial sums cos*re, cos*im, sin*re, sin*im of the same output, so
+//    the complex combine, the twiddle and the re/im interleave stay in
+//    registers (no shuffles).
+//
+//  * dft1_kernel  — N = 64: one stage with the data as the K-major A operand
+//    (rows = signals, K = 2N interleaved re/im) and the real 2N x 2N DFT
+//    matrix as B; TMEM rows are then whole output signals, staged to shared
+//    memory and written back by TMA.
+//
+// Roles (persistent CTA, one per SM): warp 0 loads tiles (TMA, or masked
+// thread loads for a partial/unaligned tile), warp 1 allocates TMEM and
+// issues MMAs from one thread, the remaining warps are epilogues.  All
+// hand-offs are mbarriers; every wait is bounded (sm100.cuh) so a stall turns
+// into an error code instead of a hung GPU.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+#include "sm100.cuh"
+
+namespace thff {
+
+// ---------------------------------------------------------------------------
+// Storage/arithmetic traits: float2 storage -> kind::tf32; half2 -> kind::f16.
+// ---------------------------------------------------------------------------
+template <bool kHalf>
+struct DType;
+
+template <>
+struct DType<false> {
+  static constexpr int kEsz = 4;                 // bytes per real
+  static constexpr int kElemsPer128B = 32;
+  static constexpr int kMmaK = 8;                // K per tcgen05.mma
+  static constexpr uint32_t kFmt = sm100::kFmtTF32;
+  // MN-major tf32 operands: 128-B rows, 32-B swizzle atoms, 4 rows per group.
+  static constexpr uint32_t kBSwizzle = 1;       // SWIZZLE_128B_BASE32B
+  static constexpr uint32_t kBSbo = 512;
+  __host__ __device__ static constexpr uint32_t swz(uint32_t o) { return o ^ (((o >> 7) & 3u) << 5); }
+};
+
+template <>
+struct DType<true> {
+  static constexpr int kEsz = 2;
+  static constexpr int kElemsPer128B = 64;
+  static constexpr int kMmaK = 16;
+  static constexpr uint32_t kFmt = sm100::kFmtF16;
+  static constexpr uint32_t kBSwizzle = sm100::kSw128;
+  static constexpr uint32_t kBSbo = 1024;
+  __host__ __device__ static constexpr uint32_t swz(uint32_t o) { return o ^ (((o >> 7) & 7u) << 4); }
+};
+
+// ---------------------------------------------------------------------------
+// Two-stage configuration per (dtype, N).
+// ---------------------------------------------------------------------------
+template <bool kHalf, int kN>
+struct Fft2Shape;
+// float2 / tf32
+template <> struct Fft2Shape<false, 128>  { static constexpr int NS = 8,  NA = 16, G1 = 4, G2 = 2, T = 32, SIN = 4; };
+template <> struct Fft2Shape<false, 256>  { static constexpr int NS = 16, NA = 16, G1 = 2, G2 = 2, T = 16, SIN = 4; };
+template <> struct Fft2Shape<false, 512>  { static constexpr int NS = 32, NA = 16, G1 = 1, G2 = 2, T = 8,  SIN = 4; };
+template <> struct Fft2Shape<false, 1024> { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 4; };
+template <> struct Fft2Shape<false, 2048> { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 3; };
+template <> struct Fft2Shape<false, 4096> { static constexpr int NS = 64, NA = 64, G1 = 1, G2 = 1, T = 1,  SIN = 2; };
+// half2 / f16
+template <> struct Fft2Shape<true, 128>   { static constexpr int NS = 4,  NA = 32, G1 = 8, G2 = 1, T = 32, SIN = 4; };
+template <> struct Fft2Shape<true, 256>   { static constexpr int NS = 8,  NA = 32, G1 = 4, G2 = 1, T = 16, SIN = 4; };
+template <> struct Fft2Shape<true, 512>   { static constexpr int NS = 16, NA = 32, G1 = 2, G2 = 1, T = 8,  SIN = 4; };
+template <> struct Fft2Shape<true, 1024>  { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 4; };
+template <> struct Fft2Shape<true, 2048>  { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 4; };
+template <> struct Fft2Shape<true, 4096>  { static constexpr int NS = 64, NA = 64, G1 = 1, G2 = 1, T = 1,  SIN = 4; };
+
+template <bool kHalf, int kN>
+struct Fft2Cfg {
+  using D = DType<kHalf>;
+  using S = Fft2Shape<kHalf, kN>;
+  static constexpr bool kIsHalf = kHalf;
+  static constexpr int N = kN, NS = S::NS, NA = S::NA, G1 = S::G1, G2 = S::G2, T = S::T, SIN = S::SIN;
+  static_assert(NS * NA == N, "factorization");
+  static constexpr int ESZ = D::kEsz, E = D::kElemsPer128B;
+  static constexpr int C1 = T / G1, C2 = T / G2;          // signals along MMA N per stage
+  static constexpr int M1 = 2 * NS * G1, M2 = 2 * NA * G2; // MMA M per stage
+  static constexpr int K1 = NS * G1, K2 = NA * G2;         // MMA K per stage
+  static constexpr int N1 = C1 * 2 * NA, N2 = C2 * 2 * NS; // MMA N per stage (TMEM columns)
+  static constexpr int H = (2 * NA * ESZ) / 128;           // 128-B atoms per signal row
+  static constexpr int TILE_BYTES = T * N * 2 * ESZ;
+  static constexpr int A1_BYTES = M1 * K1 * ESZ, A2_BYTES = M2 * K2 * ESZ;
+  static constexpr uint32_t LBO1 = K1 * 128, LBO2 = K2 * 128;  // B: stride between N-atoms
+  static constexpr int KSTEPS1 = K1 / D::kMmaK, KSTEPS2 = K2 / D::kMmaK;
+  static constexpr uint32_t KSTEP_BYTES = D::kMmaK * 128;  // B rows per MMA * 128 B
+  static_assert(M1 == 64 || M1 == 128, "M1");
+  static_assert(M2 == 64 || M2 == 128, "M2");
+  static_assert(N1 <= 256 && N2 <= 256 && N1 % 16 == 0 && N2 % 16 == 0, "N per MMA");
+  static_assert(M1 == 64 || N1 <= 128, "TMEM budget stage 1");
+  static_assert(M2 == 64 || N2 <= 128, "TMEM budget stage 2");
+  static_assert(H >= 1 && (H == 1 || G1 == 1), "TMA box needs H or G1 trivial");
+  static_assert(K1 % D::kMmaK == 0 && K2 % D::kMmaK == 0, "K");
+  // shared-memory map (offsets from a 1024-B aligned base)
+  static constexpr uint32_t OFF_A1 = 0;
+  static constexpr uint32_t OFF_A2 = (A1_BYTES + 1023) / 1024 * 1024;
+  static constexpr uint32_t OFF_IN = OFF_A2 + (A2_BYTES + 1023) / 1024 * 1024;
+  static constexpr uint32_t OFF_Y = OFF_IN + SIN * TILE_BYTES;
+  static constexpr uint32_t SMEM_DATA = OFF_Y + 2 * TILE_BYTES;
+  static constexpr uint32_t SMEM_BYTES = SMEM_DATA + 1024 /*align slack*/;
+  static_assert(SMEM_BYTES + 512 <= 232448, "shared memory budget");
+  static constexpr int kThreads = 320;                     // 10 warps
+};
+
+// Host-visible kernel parameters (besides tensor maps).
+struct FftParams {
+  const void* in;
+  void* out;
+  const void* a1;        // stage-1 A image (global), built by the host
+  const void* a2;        // stage-2 A image
+  const float2* tw;      // N-entry twiddle table exp(sign*2*pi*i*k/N) (fp32)
+  long long batch;
+  int use_tma;           // input tiles via TMA (aligned input) or thread loads
+  uint32_t* err;         // device error word (0 = ok)
+};
+
+namespace detail {
+
+template <bool kHalf>
+__device__ __forceinline__ void store_complex(uint32_t saddr, float re, float im);
+template <>
+__device__ __forceinline__ void store_complex<false>(uint32_t saddr, float re, float im) {
+  sm100::st_shared_v2(saddr, sm100::round_tf32(re), sm100::round_tf32(im));
+}
+template <>
+__device__ __forceinline__ void store_complex<true>(uint32_t saddr, float re, float im) {
+  __half2 h = __floats2half2_rn(re, im);
+  sm100::st_shared_b32(saddr, *reinterpret_cast<uint32_t*>(&h));
+}
+
+template <bool kHalf>
+__device__ __forceinline__ void store_out(void* out, long long idx, float re, float im);
+template <>
+__device__ __forceinline__ void store_out<false>(void* out, long long idx, float re, float im) {
+  reinterpret_cast<float2*>(out)[idx] = make_float2(re, im);
+}
+template <>
+__device__ __forceinline__ void store_out<true>(void* out, long long idx, float re, float im) {
+  reinterpret_cast<__half2*>(out)[idx] = __floats2half2_rn(re, im);
+}
+
+// Byte offset of complex element (sig, s, a) of a stage-1 tile in shared
+// memory (MN-major B: N-atom = column/E, K row = g*NS + s, 128-B rows).
+template <class C>
+__device__ __forceinline__ uint32_t in_tile_offset(int sig, int s, int a) {
+  const int g = sig / C::C1, c = sig % C::C1;
+  const int col = c * 2 * C::NA + 2 * a;
+  const int atom = col / C::E, e = col % C::E;
+  const uint32_t krow = g * C::NS + s;
+  return atom * C::LBO1 + C::D::swz(krow * 128u + e * C::ESZ);
+}
+
+}  // namespace detail
+
+// ---------------------------------------------------------------------------
+// Two-stage kernel
+// ---------------------------------------------------------------------------
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1)
+fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
+  using namespace sm100;
+  using D = typename C::D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN];
+  __shared__ uint64_t bar_acc1_full[2], bar_acc1_empty[2], bar_y_full[2], bar_y_empty[2];
+  __shared__ uint64_t bar_acc2_full[2], bar_acc2_empty[2], bar_const, bar_done;
+  __shared__ uint32_t tmem_slot;
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const long long batch = p.batch;
+  const long long num_tiles = (batch + C::T - 1) / C::T;
+  const long long full_tiles = batch / C::T;
+  // tiles of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int my_tiles = (int)((num_tiles > blockIdx.x) ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::SIN; ++i) { mbar_init(&bar_in_full[i], 1); mbar_init(&bar_in_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_acc1_full[i], 1); mbar_init(&bar_acc1_empty[i], 4);
+      mbar_init(&bar_y_full[i], 4);    mbar_init(&bar_y_empty[i], 1);
+      mbar_init(&bar_acc2_full[i], 1); mbar_init(&bar_acc2_empty[i], 4);
+    }
+    mbar_init(&bar_const, 1);
+    mbar_init(&bar_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) { tmem_alloc(&tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      if (p.use_tma) tma_prefetch_desc(&tmap_in);
+      // constant stage matrices (bulk copies of host-built images)
+      mbar_arrive_expect_tx(&bar_const, C::A1_BYTES + C::A2_BYTES);
+      bulk_load(smem + C::OFF_A1, p.a1, C::A1_BYTES, &bar_const);
+      bulk_load(smem + C::OFF_A2, p.a2, C::A2_BYTES, &bar_const);
+    }
+    for (int i = 0; i < my_tiles; ++i) {
+      const long long tile = blockIdx.x + (long long)i * gridDim.x;
+      const int slot = i % C::SIN;
+      const uint32_t ph = (uint32_t)(i / C::SIN) & 1u;
+      if (!mbar_wait_warp(&bar_in_empty[slot], ph ^ 1u, p.err, kDevTimeoutProducer)) break;
+      uint8_t* dst = smem + C::OFF_IN + slot * C::TILE_BYTES;
+      if (p.use_tma && tile < full_tiles) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar_in_full[slot], C::TILE_BYTES);
+          tma_load_5d(dst, &tmap_in, &bar_in_full[slot], 0, 0, 0, 0, (int)tile);
+        }
+        __syncwarp();
+      } else {
+        // masked thread loads (partial last tile or unaligned input)
+        const long long sig0 = tile * C::T;
+        const uint32_t base = smem_u32(dst);
+        for (int idx = lane; idx < C::T * C::N; idx += 32) {
+          const int sig = idx / C::N, n = idx % C::N;
+          const int s = n / C::NA, a = n % C::NA;
+          const uint32_t off = detail::in_tile_offset<C>(sig, s, a);
+          if (sig0 + sig < batch) {
+            if constexpr (C::kIsHalf) {
+              const uint32_t v = __ldg(reinterpret_cast<const unsigned int*>(p.in) + (sig0 + sig) * C::N + n);
+              st_shared_b32(base + off, v);
+            } else {
+              const float2 v = __ldg(reinterpret_cast<const float2*>(p.in) + (sig0 + sig) * C::N + n);
+              st_shared_v2(base + off, v.x, v.y);
+            }
+          } else {
+            if constexpr (C::kIsHalf) st_shared_b32(base + off, 0u);
+            else st_shared_v2(base + off, 0.f, 0.f);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_in_full[slot]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar_const, 0, p.err, kDevTimeoutMma);
+      const uint32_t a1 = smem_u32(smem + C::OFF_A1), a2 = smem_u32(smem + C::OFF_A2);
+      const uint32_t idesc1 = instr_desc(D::kFmt, C::M1, C::N1, 0, 1);
+      const uint32_t idesc2 = instr_desc(D::kFmt, C::M2, C::N2, 0, 1);
+      // A images: K-major, no swizzle, core matrix (8 rows x 16 B) contiguous;
+      // LBO = K-direction core stride = M/8 * 128 B, SBO = 128 B.
+      const uint32_t lboA1 = (C::M1 / 8) * 128, lboA2 = (C::M2 / 8) * 128;
+      for (int i = 0; ok && i <= my_tiles; ++i) {
+        if (i < my_tiles) {
+          const int slot = i % C::SIN, buf = i & 1;
+          if (!mbar_wait(&bar_in_full[slot], (uint32_t)(i / C::SIN) & 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
+          if (!mbar_wait(&bar_acc1_empty[buf], ((uint32_t)(i >> 1) & 1u) ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t b = smem_u32(smem + C::OFF_IN + slot * C::TILE_BYTES);
+          const uint32_t d = (C::M1 == 64) ? tmem + ((uint32_t)(16 * buf) << 16) : tmem + (uint32_t)(buf * C::N1);
+#pragma unroll
+          for (int k = 0; k < C::KSTEPS1; ++k) {
+            const uint64_t ad = smem_desc(a1 + k * 2 * lboA1, lboA1, 128, kSwNone);
+            const uint64_t bd = smem_desc(b + k * C::KSTEP_BYTES, C::LBO1, D::kBSbo, D::kBSwizzle);
+            if constexpr (C::kIsHalf) umma_f16(d, ad, bd, idesc1, k > 0);
+            else umma_tf32(d, ad, bd, idesc1, k > 0);
+          }
+          umma_commit(&bar_in_empty[slot]);
+          umma_commit(&bar_acc1_full[buf]);
+        }
+        if (i > 0) {
+          const int j = i - 1, buf = j & 1;
+          const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+          if (!mbar_wait(&bar_y_full[buf], ph, p.err, kDevTimeoutMma)) { ok = false; break; }
+          if (!mbar_wait(&bar_acc2_empty[buf], ph ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t b = smem_u32(smem + C::OFF_Y + buf * C::TILE_BYTES);
+          const uint32_t d = (C::M2 == 64) ? tmem + 256u + ((uint32_t)(16 * buf) << 16)
+                                           : tmem + 256u + (uint32_t)(buf * C::N2);
+#pragma unroll
+          for (int k = 0; k < C::KSTEPS2; ++k) {
+            const uint64_t ad = smem_desc(a2 + k * 2 * lboA2, lboA2, 128, kSwNone);
+            const uint64_t bd = smem_desc(b + k * C::KSTEP_BYTES, C::LBO2, D::kBSbo, D::kBSwizzle);
+            if constexpr (C::kIsHalf) umma_f16(d, ad, bd, idesc2, k > 0);
+            else umma_tf32(d, ad, bd, idesc2, k > 0);
+          }
+          umma_commit(&bar_y_empty[buf]);
+          umma_commit(&bar_acc2_full[buf]);
+        }
+      }
+      // drain: all issued MMAs complete before TMEM is released
+      umma_commit(&bar_done);
+      mbar_wait(&bar_done, 0, p.err, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue 1
+    // quadrant q holds TMEM lanes [32q, 32q+32); M=64 -> row block q at lanes
+    // 32q + 16*buf; M=128 -> row blocks 2q, 2q+1 at lanes 32q, 32q+16.
+    const uint32_t q = warp & 3u;
+    constexpr int kBlocks = C::M1 / 64;  // row blocks per warp (1 or 2)
+    constexpr int kTwPerBlock = C::NA / 4 > 0 ? C::NA / 4 : 1;
+    float2 tw[kBlocks][kTwPerBlock];
+    // row pair rp = block*8 + lane/4 -> (g1, ks); column complex index
+    // p = 4J + lane%4 -> (c1, a) with a = p % NA in {lane%4 + 4i}.
+#pragma unroll
+    for (int bi = 0; bi < kBlocks; ++bi) {
+      const int block = (C::M1 == 64) ? (int)q : (int)(2 * q + bi);
+      const int rp = block * 8 + (int)(lane >> 2);
+      const int ks = rp % C::NS;
+#pragma unroll
+      for (int i = 0; i < kTwPerBlock; ++i) {
+        const int a = (int)(lane & 3u) + 4 * i;
+        tw[bi][i] = p.tw[(a * ks) % C::N];
+      }
+    }
+    const uint32_t ybase = smem_u32(smem + C::OFF_Y);
+    for (int i = 0; i < my_tiles; ++i) {
+      const int buf = i & 1;
+      const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+      if (!mbar_wait_warp(&bar_acc1_full[buf], ph, p.err, kDevTimeoutEpilogue)) break;
+      if (!mbar_wait_warp(&bar_y_empty[buf], ph ^ 1u, p.err, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t yb = ybase + buf * C::TILE_BYTES;
+#pragma unroll
+      for (int bi = 0; bi < kBlocks; ++bi) {
+        const int block = (C::M1 == 64) ? (int)q : (int)(2 * q + bi);
+        const uint32_t lane_base = (C::M1 == 64) ? 32u * q + 16u * buf : 32u * q + 16u * bi;
+        const uint32_t col_base = (C::M1 == 64) ? 0u : (uint32_t)(buf * C::N1);
+        const int rp = block * 8 + (int)(lane >> 2);
+        const int g1 = rp / C::NS, ks = rp % C::NS;
+#pragma unroll
+        for (int chunk = 0; chunk < C::N1 / 64; ++chunk) {
+          uint32_t r[32];
+          tmem_ld_16x256b_x8(tmem + (lane_base << 16) + col_base + chunk * 64, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int pidx = 4 * (chunk * 8 + j) + (int)(lane & 3u);
+            const int c1 = pidx / C::NA, a = pidx % C::NA;
+            const float rr = __uint_as_float(r[4 * j + 0]), ri = __uint_as_float(r[4 * j + 1]);
+            const float ir = __uint_as_float(r[4 * j + 2]), ii = __uint_as_float(r[4 * j + 3]);
+            const float yr = rr - ii, yi = ir + ri;
+            const float2 w = tw[bi][(chunk * 8 + j) % kTwPerBlock];
+            const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
+            const int sig = g1 * C::C1 + c1;
+            const int g2 = sig / C::C2, c2 = sig % C::C2;
+            const uint32_t krow = g2 * C::NA + a;
+            const int col = c2 * 2 * C::NS + 2 * ks;
+            const uint32_t off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
+            detail::store_complex<C::kIsHalf>(yb + off, zr, zi);
+          }
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) { mbar_arrive(&bar_acc1_empty[buf]); mbar_arrive(&bar_y_full[buf]); }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue 2
+    const uint32_t q = warp & 3u;
+    constexpr int kBlocks = C::M2 / 64;
+    for (int i = 0; i < my_tiles; ++i) {
+      const long long tile = blockIdx.x + (long long)i * gridDim.x;
+      const int buf = i & 1;
+      const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+      if (!mbar_wait_warp(&bar_acc2_full[buf], ph, p.err, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const long long sig0 = tile * C::T;
+#pragma unroll
+      for (int bi = 0; bi < kBlocks; ++bi) {
+        const int block = (C::M2 == 64) ? (int)q : (int)(2 * q + bi);
+        const uint32_t lane_base = (C::M2 == 64) ? 32u * q + 16u * buf : 32u * q + 16u * bi;
+        const uint32_t col_base = 256u + ((C::M2 == 64) ? 0u : (uint32_t)(buf * C::N2));
+        const int rp = block * 8 + (int)(lane >> 2);
+        const int g2 = rp / C::NA, ka = rp % C::NA;
+#pragma unroll
+        for (int chunk = 0; chunk < C::N2 / 64; ++chunk) {
+          uint32_t r[32];
+          tmem_ld_16x256b_x8(tmem + (lane_base << 16) + col_base + chunk * 64, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int pidx = 4 * (chunk * 8 + j) + (int)(lane & 3u);
+            const int c2 = pidx / C::NS, ks = pidx % C::NS;
+            const float rr = __uint_as_float(r[4 * j + 0]), ri = __uint_as_float(r[4 * j + 1]);
+            const float ir = __uint_as_float(r[4 * j + 2]), ii = __uint_as_float(r[4 * j + 3]);
+            const long long sig = sig0 + g2 * C::C2 + c2;
+            if (sig < batch)
+              detail::store_out<C::kIsHalf>(p.out, sig * C::N + (long long)C::NS * ka + ks, rr - ii, ir + ri);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_acc2_empty[buf]);
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One-stage kernel for N = 64: data tile (128 signals) is the K-major A
+// operand, the real 128 x 128 DFT matrix (rows (k, re|im), K = (j, re|im))
+// is B.  TMEM row = one signal's full interleaved output.
+// ---------------------------------------------------------------------------
+template <bool kHalf>
+struct Dft1Cfg {
+  using D = DType<kHalf>;
+  static constexpr bool kIsHalf = kHalf;
+  static constexpr int N = 64, T = 128;                 // signals per tile = MMA M
+  static constexpr int ESZ = D::kEsz, E = D::kElemsPer128B;
+  static constexpr int KATOMS = (2 * N * ESZ) / 128;     // 128-B K atoms per row
+  static constexpr int TILE_BYTES = T * 2 * N * ESZ;      // also the B size
+  static constexpr int B_BYTES = 2 * N * 2 * N * ESZ;
+  static constexpr int KSTEPS = 2 * N / D::kMmaK;
+  static constexpr int SIN = kHalf ? 4 : 2;
+  static constexpr uint32_t OFF_B = 0;
+  static constexpr uint32_t OFF_IN = B_BYTES;
+  static constexpr uint32_t SMEM_BYTES = OFF_IN + SIN * TILE_BYTES + 1024;
+  static_assert(SMEM_BYTES + 512 <= 232448, "shared memory budget");
+  static constexpr int kThreads = 192;                   // producer, MMA, 4 epilogue warps
+};
+
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1)
+dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__ CUtensorMap tmap_out,
+            const FftParams p, int use_tma_store) {
+  using namespace sm100;
+  using D = typename C::D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN];
+  __shared__ uint64_t bar_acc_full[2], bar_acc_empty[2], bar_staged[2], bar_const, bar_done;
+  __shared__ uint32_t tmem_slot;
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const long long batch = p.batch;
+  const long long num_tiles = (batch + C::T - 1) / C::T;
+  const int my_tiles = (int)((num_tiles > blockIdx.x) ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::SIN; ++i) { mbar_init(&bar_in_full[i], 1); mbar_init(&bar_in_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_acc_full[i], 1); mbar_init(&bar_acc_empty[i], 4); mbar_init(&bar_staged[i], 4);
+    }
+    mbar_init(&bar_const, 1);
+    mbar_init(&bar_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) { tmem_alloc(&tmem_slot, 256); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  // element (sig, col) of a tile: K-major SW128, [katom][sig][128 B]
+  auto tile_off = [](int sig, int col) -> uint32_t {
+    return (uint32_t)(col / C::E) * (C::T * 128u) + sw128((uint32_t)sig * 128u + (col % C::E) * C::ESZ);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      if (p.use_tma) tma_prefetch_desc(&tmap_in);
+      mbar_arrive_expect_tx(&bar_const, C::B_BYTES);
+      bulk_load(smem + C::OFF_B, p.a1, C::B_BYTES, &bar_const);
+    }
+    for (int i = 0; i < my_tiles; ++i) {
+      const long long tile = blockIdx.x + (long long)i * gridDim.x;
+      const int slot = i % C::SIN;
+      if (!mbar_wait_warp(&bar_in_empty[slot], ((uint32_t)(i / C::SIN) & 1u) ^ 1u, p.err, kDevTimeoutProducer)) break;
+      uint8_t* dst = smem + C::OFF_IN + slot * C::TILE_BYTES;
+      if (p.use_tma) {
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar_in_full[slot], C::TILE_BYTES);
+          tma_load_3d(dst, &tmap_in, &bar_in_full[slot], 0, (int)(tile * C::T), 0);
+        }
+        __syncwarp();
+      } else {
+        const long long sig0 = tile * C::T;
+        const uint32_t base = smem_u32(dst);
+        for (int idx = lane; idx < C::T * C::N; idx += 32) {
+          const int sig = idx / C::N, n = idx % C::N;
+          const uint32_t off = tile_off(sig, 2 * n);
+          if (sig0 + sig < batch) {
+            if constexpr (C::kIsHalf) {
+              st_shared_b32(base + off, __ldg(reinterpret_cast<const unsigned int*>(p.in) + (sig0 + sig) * C::N + n));
+            } else {
+              const float2 v = __ldg(reinterpret_cast<const float2*>(p.in) + (sig0 + sig) * C::N + n);
+              st_shared_v2(base + off, v.x, v.y);
+            }
+          } else {
+            if constexpr (C::kIsHalf) st_shared_b32(base + off, 0u);
+            else st_shared_v2(base + off, 0.f, 0.f);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_in_full[slot]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar_const, 0, p.err, kDevTimeoutMma);
+      const uint32_t bsm = smem_u32(smem + C::OFF_B);
+      const uint32_t idesc = instr_desc(D::kFmt, 128, 2 * C::N, 0, 0);
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        const int slot = i % C::SIN, buf = i & 1;
+        if (!mbar_wait(&bar_in_full[slot], (uint32_t)(i / C::SIN) & 1u, p.err, kDevTimeoutMma)) break;
+        if (!mbar_wait(&bar_acc_empty[buf], ((uint32_t)(i >> 1) & 1u) ^ 1u, p.err, kDevTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + C::OFF_IN + slot * C::TILE_BYTES);
+        const uint32_t d = tmem + (uint32_t)(buf * 128);
+        constexpr int kStepsPerAtom = 128 / (D::kMmaK * C::ESZ);
+#pragma unroll
+        for (int k = 0; k < C::KSTEPS; ++k) {
+          const int ka = k / kStepsPerAtom, kin = k % kStepsPerAtom;
+          const uint32_t koff = ka * (C::T * 128u) + kin * 32u;
+          const uint64_t ad = smem_desc(a + koff, 16, 1024, kSw128);
+          const uint64_t bd = smem_desc(bsm + koff, 16, 1024, kSw128);
+          if constexpr (C::kIsHalf) umma_f16(d, ad, bd, idesc, k > 0);
+          else umma_tf32(d, ad, bd, idesc, k > 0);
+        }
+        umma_commit(&bar_acc_full[buf]);
+      }
+      umma_commit(&bar_done);
+      mbar_wait(&bar_done, 0, p.err, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else {
+    // epilogue: warp -> quadrant q = warp & 3, thread = signal 32q + lane
+    const uint32_t q = warp & 3u;
+    int pending_slot = -1;
+    for (int i = 0; i < my_tiles; ++i) {
+      const long long tile = blockIdx.x + (long long)i * gridDim.x;
+      const int slot = i % C::SIN, buf = i & 1;
+      if (!mbar_wait_warp(&bar_acc_full[buf], (uint32_t)(i >> 1) & 1u, p.err, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      // the MMA that filled acc[buf] has finished reading in[slot]; reuse it
+      // as the output staging tile.
+      uint8_t* stage = smem + C::OFF_IN + slot * C::TILE_BYTES;
+      const uint32_t sbase = smem_u32(stage);
+      const int sig = (int)(32 * q + lane);
+      const long long gsig = tile * C::T + sig;
+#pragma unroll 1
+      for (int chunk = 0; chunk < 4; ++chunk) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + ((32u * q) << 16) + (uint32_t)(buf * 128 + chunk * 32), r);
+        tmem_wait_ld();
+        if (use_tma_store) {
+          if constexpr (C::kIsHalf) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t h[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                __half2 t2 = __floats2half2_rn(__uint_as_float(r[8 * v + 2 * u]), __uint_as_float(r[8 * v + 2 * u + 1]));
+                h[u] = *reinterpret_cast<uint32_t*>(&t2);
+              }
+              st_shared_v4(sbase + tile_off(sig, chunk * 32 + 8 * v), h[0], h[1], h[2], h[3]);
+            }
+          } else {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              st_shared_v4(sbase + tile_off(sig, chunk * 32 + 4 * v), r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          }
+        } else if (gsig < batch) {
+#pragma unroll
+          for (int u = 0; u < 16; ++u)
+            detail::store_out<C::kIsHalf>(p.out, gsig * C::N + chunk * 16 + u, __uint_as_float(r[2 * u]),
+                                          __uint_as_float(r[2 * u + 1]));
+        }
+      }
+      // Hand-off: each epilogue warp arrives on staged[buf] after its part of
+      // the tile is in shared memory (and visible to the async proxy); one
+      // thread then stores the tile and, one tile later, releases the
+      // staging slot back to the producer.
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) { mbar_arrive(&bar_acc_empty[buf]); mbar_arrive(&bar_staged[buf]); }
+      if (warp == 2) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(&bar_staged[buf], (uint32_t)(i >> 1) & 1u, p.err, kDevTimeoutEpilogue);
+        if (!__shfl_sync(0xffffffffu, (int)ok, 0)) break;
+        if (lane == 0) {
+          if (use_tma_store) {
+            tma_store_3d(&tmap_out, stage, 0, (int)(tile * C::T), 0);
+            bulk_commit_group();
+            bulk_wait_group_read<1>();   // the previous tile's store has read its slot
+          }
+          if (pending_slot >= 0) mbar_arrive(&bar_in_empty[pending_slot]);
+        }
+        pending_slot = slot;
+      }
+      __syncwarp();
+    }
+    if (warp == 2 && lane == 0) {
+      if (use_tma_store) bulk_wait_group<0>();
+      if (pending_slot >= 0) mbar_arrive(&bar_in_empty[pending_slot]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace thff

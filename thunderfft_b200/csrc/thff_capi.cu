@@ -1,0 +1,497 @@
+// thff_capi.cu — C ABI of libthunderfft_b200.so (declared in include/thff.h).
+//
+// Host side of the batched C2C FFT: argument contract of the reference's
+// ThunderFFT_global wrapper (include/thunderfft/detail/thunderfft_impl_kernel.cuh:6-41),
+// the reference-compatible twiddle cache (thunderfft_impl_twiddle.cuh:26-378),
+// per-device FFT constants (stage DFT matrices in the UMMA operand layouts the
+// kernels read, twiddle tables), TMA tensor maps and kernel launches.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/thff.h"
+#include "fft_kernels.cuh"
+
+namespace {
+
+constexpr double kTau = 6.283185307179586476925286766559;
+
+thread_local std::string g_last_error;
+
+thff_status fail(thff_status st, const std::string& msg) {
+  g_last_error = msg;
+  return st;
+}
+
+thff_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(THFF_CUDA_ERROR, std::string("[ThunderFFT] ") + what + ": " + cudaGetErrorString(e));
+}
+
+#define THFF_CUDA(expr, what)                      \
+  do {                                             \
+    cudaError_t e_ = (expr);                       \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+bool valid_n(int n) {
+  return n == 64 || n == 128 || n == 256 || n == 512 || n == 1024 || n == 2048 || n == 4096;
+}
+bool valid_dtype(int dt) { return dt == THFF_F32 || dt == THFF_F16; }
+
+// ---------------------------------------------------------------------------
+// Host-side value encodings
+// ---------------------------------------------------------------------------
+uint32_t f32_bits(float f) { uint32_t u; std::memcpy(&u, &f, 4); return u; }
+float bits_f32(uint32_t u) { float f; std::memcpy(&f, &u, 4); return f; }
+
+// Round to the nearest TF32 value (10 explicit mantissa bits), ties away —
+// the tensor core would otherwise truncate the low 13 bits.
+float tf32_rn(float x) {
+  uint32_t u = f32_bits(x);
+  if ((u & 0x7f800000u) == 0x7f800000u) return x;
+  u = (u + 0x1000u) & 0xffffe000u;
+  return bits_f32(u);
+}
+
+void put_value(std::vector<uint8_t>& img, size_t off, double v, bool half) {
+  if (half) {
+    const __half h = __float2half_rn(float(v));
+    std::memcpy(img.data() + off, &h, 2);
+  } else {
+    const float f = tf32_rn(float(v));
+    std::memcpy(img.data() + off, &f, 4);
+  }
+}
+
+// Byte offset of element (m, k) of an M x K K-major operand without swizzle:
+// 8x16-byte core matrices stored contiguously, core (m/8, kbyte/16) at
+// ((kbyte/16) * (M/8) + m/8) * 128.
+size_t kmajor_noswz_off(int m, int k, int M, int esz) {
+  const int kb = k * esz;
+  return size_t((kb / 16) * (M / 8) + m / 8) * 128 + (m % 8) * 16 + (kb % 16);
+}
+
+// Stage DFT matrix of length L for G signal groups (block diagonal):
+// rows (g, ks, re|im) laid out in 16-row blocks [8 cos rows | 8 sin rows],
+// rp = g*L + ks, row = 16*(rp/8) + 8*c + rp%8; columns k = g*L + s.
+//   row (rp, 0): cos(theta), row (rp, 1): sin(theta), theta = sign*2*pi*s*ks/L
+std::vector<uint8_t> build_stage_matrix(int L, int G, int sign, bool half) {
+  const int esz = half ? 2 : 4;
+  const int M = 2 * L * G, K = L * G;
+  std::vector<uint8_t> img(size_t(M) * K * esz, 0);
+  for (int g = 0; g < G; ++g)
+    for (int ks = 0; ks < L; ++ks) {
+      const int rp = g * L + ks;
+      for (int c = 0; c < 2; ++c) {
+        const int m = 16 * (rp / 8) + 8 * c + rp % 8;
+        for (int s = 0; s < L; ++s) {
+          const double th = sign * kTau * double((s * ks) % L) / double(L);
+          put_value(img, kmajor_noswz_off(m, g * L + s, M, esz), c == 0 ? std::cos(th) : std::sin(th), half);
+        }
+      }
+    }
+  return img;
+}
+
+// Real 2N x 2N DFT matrix for the one-stage kernel, K-major with 128-B
+// swizzle: row n = 2k + c_out, column K = 2j + c_in, stored
+// [K/E][row][128 B] with the 16-B chunk index XORed by (row % 8).
+std::vector<uint8_t> build_dft1_matrix(int N, int sign, bool half) {
+  const int esz = half ? 2 : 4, E = 128 / esz, R = 2 * N;
+  std::vector<uint8_t> img(size_t(R) * R * esz, 0);
+  for (int n = 0; n < R; ++n)
+    for (int K = 0; K < R; ++K) {
+      const int k = n / 2, co = n % 2, j = K / 2, ci = K % 2;
+      const double th = sign * kTau * double((j * k) % N) / double(N);
+      const double c = std::cos(th), s = std::sin(th);
+      const double v = (co == 0) ? (ci == 0 ? c : -s) : (ci == 0 ? s : c);
+      const uint32_t within = uint32_t(n) * 128u + uint32_t(K % E) * esz;
+      const size_t off = size_t(K / E) * (size_t(R) * 128) + thff::sm100::sw128(within);
+      put_value(img, off, v, half);
+    }
+  return img;
+}
+
+// ---------------------------------------------------------------------------
+// Per-device state
+// ---------------------------------------------------------------------------
+struct DevBuf {
+  void* p = nullptr;
+  ~DevBuf() {}
+};
+
+struct Consts {            // per (dtype, N, direction)
+  void* a1 = nullptr;      // stage-1 A image (or the one-stage DFT matrix)
+  void* a2 = nullptr;      // stage-2 A image
+  void* tw = nullptr;      // float2 twiddles exp(sign 2 pi i k / N)
+};
+
+struct RefCache {          // reference-compatible twiddle cache entry
+  void* dW = nullptr;
+  int n = 0;
+};
+
+struct DeviceState {
+  bool ready = false;
+  int sms = 0;
+  uint32_t* d_err = nullptr;
+  std::map<int, Consts> consts;  // key = (dtype*2 + fwd)*8192 + N
+  RefCache ref[2];
+  std::map<const void*, bool> attr_done;
+};
+
+std::mutex g_mutex;
+std::map<int, DeviceState> g_dev;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+thread_local uint32_t* t_err_host = nullptr;  // pinned readback word per thread
+
+thff_status current_device(int* dev) {
+  THFF_CUDA(cudaGetDevice(dev), "cudaGetDevice");
+  return THFF_OK;
+}
+
+thff_status ensure_device(int dev, DeviceState** out) {
+  DeviceState& st = g_dev[dev];
+  if (!st.ready) {
+    cudaDeviceProp prop;
+    THFF_CUDA(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties");
+    if (prop.major != 10)
+      return fail(THFF_UNSUPPORTED, std::string("[ThunderFFT] this build targets sm_100a (B200); device is ") +
+                                        prop.name + " sm_" + std::to_string(prop.major) + std::to_string(prop.minor));
+    st.sms = prop.multiProcessorCount;
+    THFF_CUDA(cudaMalloc(&st.d_err, sizeof(uint32_t)), "cudaMalloc(error word)");
+    THFF_CUDA(cudaMemset(st.d_err, 0, sizeof(uint32_t)), "cudaMemset(error word)");
+    if (!g_encode) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      THFF_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q),
+                "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+      if (!fn || q != cudaDriverEntryPointSuccess)
+        return fail(THFF_CUDA_ERROR, "[ThunderFFT] cuTensorMapEncodeTiled unavailable");
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    st.ready = true;
+  }
+  *out = &st;
+  return THFF_OK;
+}
+
+thff_status upload(const std::vector<uint8_t>& img, void** dst) {
+  THFF_CUDA(cudaMalloc(dst, img.size()), "cudaMalloc(FFT constants)");
+  THFF_CUDA(cudaMemcpy(*dst, img.data(), img.size(), cudaMemcpyHostToDevice), "cudaMemcpy(FFT constants)");
+  return THFF_OK;
+}
+
+template <bool kHalf, int kN>
+struct ShapeOf {
+  static constexpr int NS = thff::Fft2Shape<kHalf, kN>::NS, NA = thff::Fft2Shape<kHalf, kN>::NA;
+  static constexpr int G1 = thff::Fft2Shape<kHalf, kN>::G1, G2 = thff::Fft2Shape<kHalf, kN>::G2;
+};
+
+thff_status build_consts(int dtype, int n, bool fwd, Consts* c) {
+  const bool half = dtype == THFF_F16;
+  const int sign = fwd ? -1 : 1;
+  thff_status st;
+  if (n == 64) {
+    if ((st = upload(build_dft1_matrix(64, sign, half), &c->a1)) != THFF_OK) return st;
+  } else {
+    int NS = 0, NA = 0, G1 = 0, G2 = 0;
+#define THFF_SHAPE(H, NN)                                                                      \
+  if (half == H && n == NN) {                                                                  \
+    NS = ShapeOf<H, NN>::NS; NA = ShapeOf<H, NN>::NA; G1 = ShapeOf<H, NN>::G1; G2 = ShapeOf<H, NN>::G2; \
+  }
+    THFF_SHAPE(false, 128) THFF_SHAPE(false, 256) THFF_SHAPE(false, 512) THFF_SHAPE(false, 1024)
+    THFF_SHAPE(false, 2048) THFF_SHAPE(false, 4096) THFF_SHAPE(true, 128) THFF_SHAPE(true, 256)
+    THFF_SHAPE(true, 512) THFF_SHAPE(true, 1024) THFF_SHAPE(true, 2048) THFF_SHAPE(true, 4096)
+#undef THFF_SHAPE
+    if ((st = upload(build_stage_matrix(NS, G1, sign, half), &c->a1)) != THFF_OK) return st;
+    if ((st = upload(build_stage_matrix(NA, G2, sign, half), &c->a2)) != THFF_OK) return st;
+  }
+  std::vector<uint8_t> tw(size_t(n) * 8);
+  for (int k = 0; k < n; ++k) {
+    const double th = sign * kTau * double(k) / double(n);
+    const float v[2] = {float(std::cos(th)), float(std::sin(th))};
+    std::memcpy(tw.data() + size_t(k) * 8, v, 8);
+  }
+  return upload(tw, &c->tw);
+}
+
+thff_status get_consts(DeviceState& st, int dtype, int n, bool fwd, const Consts** out) {
+  const int key = (dtype * 2 + (fwd ? 1 : 0)) * 8192 + n;
+  auto it = st.consts.find(key);
+  if (it == st.consts.end()) {
+    Consts c;
+    thff_status s = build_consts(dtype, n, fwd, &c);
+    if (s != THFF_OK) return s;
+    it = st.consts.emplace(key, c).first;
+  }
+  *out = &it->second;
+  return THFF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Launch helpers
+// ---------------------------------------------------------------------------
+thff_status encode(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                   const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                   CUtensorMapSwizzle swz) {
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) { gd[i] = dims[i]; bx[i] = box[i]; es[i] = 1; }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
+  CUresult r = g_encode(map, dt, rank, const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(THFF_CUDA_ERROR, "[ThunderFFT] cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return THFF_OK;
+}
+
+template <class K>
+thff_status set_smem_attr(DeviceState& st, K kernel, int bytes) {
+  const void* key = reinterpret_cast<const void*>(kernel);
+  if (!st.attr_done[key]) {
+    THFF_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+              "cudaFuncSetAttribute(max dynamic shared memory)");
+    st.attr_done[key] = true;
+  }
+  return THFF_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <bool kHalf, int kN>
+thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* out, long long batch,
+                        cudaStream_t stream) {
+  using C = thff::Fft2Cfg<kHalf, kN>;
+  const long long num_tiles = (batch + C::T - 1) / C::T;
+  const long long full_tiles = batch / C::T;
+  const bool use_tma = aligned16(in);
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  {
+    const uint64_t sig_bytes = uint64_t(C::N) * 2 * C::ESZ;
+    uint64_t dims[5], strides[4];
+    uint32_t box[5];
+    dims[0] = C::E;            box[0] = C::E;
+    dims[1] = C::NS;           box[1] = C::NS;     strides[0] = uint64_t(2 * C::NA * C::ESZ);
+    if (C::H > 1) { dims[2] = C::H;  box[2] = C::H;  strides[1] = 128; }
+    else if (C::G1 > 1) { dims[2] = C::G1; box[2] = C::G1; strides[1] = uint64_t(C::C1) * sig_bytes; }
+    else { dims[2] = 1; box[2] = 1; strides[1] = 128; }
+    dims[3] = C::C1;           box[3] = C::C1;     strides[2] = sig_bytes;
+    dims[4] = uint64_t(full_tiles > 0 ? full_tiles : 1); box[4] = 1;
+    strides[3] = uint64_t(C::T) * sig_bytes;
+    thff_status s = encode(&map, kHalf ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5,
+                           in, dims, strides, box,
+                           kHalf ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (s != THFF_OK) return s;
+  }
+  thff::FftParams p;
+  p.in = in; p.out = out; p.a1 = c.a1; p.a2 = c.a2; p.tw = reinterpret_cast<const float2*>(c.tw);
+  p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = st.d_err;
+  auto kernel = thff::fft2_kernel<C>;
+  thff_status s = set_smem_attr(st, kernel, int(C::SMEM_BYTES));
+  if (s != THFF_OK) return s;
+  const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
+  kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map, p);
+  THFF_CUDA(cudaGetLastError(), "ThunderFFT_global launch");
+  return THFF_OK;
+}
+
+template <bool kHalf>
+thff_status launch_dft1(DeviceState& st, const Consts& c, const void* in, void* out, long long batch,
+                        cudaStream_t stream) {
+  using C = thff::Dft1Cfg<kHalf>;
+  const long long num_tiles = (batch + C::T - 1) / C::T;
+  const bool use_tma = aligned16(in);
+  const bool tma_store = aligned16(out);
+  CUtensorMap map_in, map_out;
+  std::memset(&map_in, 0, sizeof(map_in));
+  std::memset(&map_out, 0, sizeof(map_out));
+  const uint64_t dims[3] = {uint64_t(C::E), uint64_t(batch), uint64_t(C::KATOMS)};
+  const uint64_t strides[2] = {uint64_t(2 * C::N * C::ESZ), 128};
+  const uint32_t box[3] = {uint32_t(C::E), uint32_t(C::T), uint32_t(C::KATOMS)};
+  const CUtensorMapDataType dt = kHalf ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  thff_status s;
+  if (use_tma && (s = encode(&map_in, dt, 3, in, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) != THFF_OK) return s;
+  if (tma_store && (s = encode(&map_out, dt, 3, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) != THFF_OK) return s;
+  thff::FftParams p;
+  p.in = in; p.out = out; p.a1 = c.a1; p.a2 = nullptr; p.tw = nullptr;
+  p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = st.d_err;
+  auto kernel = thff::dft1_kernel<C>;
+  if ((s = set_smem_attr(st, kernel, int(C::SMEM_BYTES))) != THFF_OK) return s;
+  const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
+  kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map_in, map_out, p, tma_store ? 1 : 0);
+  THFF_CUDA(cudaGetLastError(), "ThunderFFT_global launch");
+  return THFF_OK;
+}
+
+thff_status dispatch_c2c(DeviceState& st, const Consts& c, int dtype, int n, const void* in, void* out,
+                         long long batch, cudaStream_t stream) {
+  const bool half = dtype == THFF_F16;
+  switch (n) {
+    case 64: return half ? launch_dft1<true>(st, c, in, out, batch, stream) : launch_dft1<false>(st, c, in, out, batch, stream);
+    case 128: return half ? launch_fft2<true, 128>(st, c, in, out, batch, stream) : launch_fft2<false, 128>(st, c, in, out, batch, stream);
+    case 256: return half ? launch_fft2<true, 256>(st, c, in, out, batch, stream) : launch_fft2<false, 256>(st, c, in, out, batch, stream);
+    case 512: return half ? launch_fft2<true, 512>(st, c, in, out, batch, stream) : launch_fft2<false, 512>(st, c, in, out, batch, stream);
+    case 1024: return half ? launch_fft2<true, 1024>(st, c, in, out, batch, stream) : launch_fft2<false, 1024>(st, c, in, out, batch, stream);
+    case 2048: return half ? launch_fft2<true, 2048>(st, c, in, out, batch, stream) : launch_fft2<false, 2048>(st, c, in, out, batch, stream);
+    case 4096: return half ? launch_fft2<true, 4096>(st, c, in, out, batch, stream) : launch_fft2<false, 4096>(st, c, in, out, batch, stream);
+  }
+  return fail(THFF_INVALID_ARGUMENT, "[ThunderFFT] unsupported FFT length");
+}
+
+thff_status read_device_error(DeviceState& st, cudaStream_t stream) {
+  if (!t_err_host) THFF_CUDA(cudaMallocHost(&t_err_host, sizeof(uint32_t)), "cudaMallocHost(error word)");
+  *t_err_host = 0;
+  THFF_CUDA(cudaMemcpyAsync(t_err_host, st.d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
+            "cudaMemcpyAsync(error word)");
+  THFF_CUDA(cudaStreamSynchronize(stream), "ThunderFFT_global synchronize");
+  if (*t_err_host != 0) {
+    const uint32_t code = *t_err_host;
+    cudaMemsetAsync(st.d_err, 0, sizeof(uint32_t), stream);
+    cudaStreamSynchronize(stream);
+    return fail(THFF_DEVICE_TIMEOUT, "[ThunderFFT] device pipeline wait timed out (code " + std::to_string(code) + ")");
+  }
+  return THFF_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* thff_version(void) { return "thunderfft_b200 0.1 (sm_100a tcgen05/TMA)"; }
+
+const char* thff_last_error(void) { return g_last_error.c_str(); }
+
+thff_status thff_initialize(int dtype, int n) {
+  if (!valid_dtype(dtype)) return fail(THFF_INVALID_ARGUMENT, "ThunderFFTInitialize<T>: supported T are float and half only");
+  if (!valid_n(n)) return fail(THFF_INVALID_ARGUMENT, "ThunderFFTInitialize<T>: unsupported FFT size");
+  std::lock_guard<std::mutex> lock(g_mutex);
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  DeviceState* st;
+  if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
+  RefCache& rc = st->ref[dtype];
+  if (!(rc.dW && rc.n == n)) {
+    if (rc.dW) {
+      rc.n = 0;
+      THFF_CUDA(cudaFree(rc.dW), "cudaFree cached twiddle (initialize)");
+      rc.dW = nullptr;
+    }
+    // W[k] = (cos 2 pi k / N, sin 2 pi k / N) (positive angle, as the
+    // reference's preprocess_W_*: thunderfft_impl_twiddle.cuh:76-114).
+    const bool half = dtype == THFF_F16;
+    std::vector<uint8_t> h(size_t(n) * (half ? 4 : 8));
+    for (int k = 0; k < n; ++k) {
+      const double th = kTau * double(k) / double(n);
+      if (half) {
+        const __half2 v = __halves2half2(__float2half_rn(float(std::cos(th))), __float2half_rn(float(std::sin(th))));
+        std::memcpy(h.data() + size_t(k) * 4, &v, 4);
+      } else {
+        const float v[2] = {float(std::cos(th)), float(std::sin(th))};
+        std::memcpy(h.data() + size_t(k) * 8, v, 8);
+      }
+    }
+    void* d = nullptr;
+    if ((s = upload(h, &d)) != THFF_OK) return s;
+    rc.dW = d;
+    rc.n = n;
+  }
+  // FFT constants for both directions of this length.
+  const Consts* c;
+  if ((s = get_consts(*st, dtype, n, true, &c)) != THFF_OK) return s;
+  if ((s = get_consts(*st, dtype, n, false, &c)) != THFF_OK) return s;
+  return THFF_OK;
+}
+
+thff_status thff_finalize(int dtype) {
+  if (!valid_dtype(dtype)) return fail(THFF_INVALID_ARGUMENT, "ThunderFFTFinalize<T>: supported T are float and half only");
+  std::lock_guard<std::mutex> lock(g_mutex);
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  auto it = g_dev.find(dev);
+  if (it == g_dev.end()) return THFF_OK;
+  RefCache& rc = it->second.ref[dtype];
+  rc.n = 0;
+  if (rc.dW) {
+    void* d = rc.dW;
+    rc.dW = nullptr;
+    THFF_CUDA(cudaFree(d), "cudaFree cached twiddle (finalize)");
+  }
+  return THFF_OK;
+}
+
+thff_status thff_twiddle_table(int dtype, const void** table, int* n) {
+  if (!valid_dtype(dtype) || !table || !n) return fail(THFF_INVALID_ARGUMENT, "thff_twiddle_table: bad arguments");
+  std::lock_guard<std::mutex> lock(g_mutex);
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  auto it = g_dev.find(dev);
+  *table = (it == g_dev.end()) ? nullptr : it->second.ref[dtype].dW;
+  *n = (it == g_dev.end()) ? 0 : it->second.ref[dtype].n;
+  return THFF_OK;
+}
+
+thff_status thff_c2c_async(int dtype, int n, int forward, const void* d_input, void* d_output,
+                           long long batch, void* stream) {
+  if (!valid_dtype(dtype)) return fail(THFF_INVALID_ARGUMENT, "ThunderFFT_global supports float and half only");
+  if (!valid_n(n)) return fail(THFF_INVALID_ARGUMENT, "Unsupported ThunderFFT length");
+  if (batch < 0) return fail(THFF_INVALID_ARGUMENT, "ThunderFFT batch must be nonnegative");
+  if (batch == 0) return THFF_OK;
+  if (!d_input || !d_output || d_input == d_output)
+    return fail(THFF_INVALID_ARGUMENT, "ThunderFFT requires separate non-null input/output buffers");
+  const size_t esz = dtype == THFF_F16 ? 4 : 8;
+  const uintptr_t a = reinterpret_cast<uintptr_t>(d_input), b = reinterpret_cast<uintptr_t>(d_output);
+  const uintptr_t bytes = uintptr_t(batch) * uintptr_t(n) * esz;
+  if (a < b + bytes && b < a + bytes)
+    return fail(THFF_INVALID_ARGUMENT, "ThunderFFT requires separate non-null input/output buffers");
+  if ((a % esz) || (b % esz)) return fail(THFF_INVALID_ARGUMENT, "ThunderFFT buffers must be aligned to the complex element size");
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  DeviceState* st;
+  const Consts* c;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
+    if ((s = get_consts(*st, dtype, n, forward != 0, &c)) != THFF_OK) return s;
+  }
+  return dispatch_c2c(*st, *c, dtype, n, d_input, d_output, batch, reinterpret_cast<cudaStream_t>(stream));
+}
+
+thff_status thff_sync_check(void* stream) {
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  DeviceState* st;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
+  }
+  return read_device_error(*st, reinterpret_cast<cudaStream_t>(stream));
+}
+
+thff_status thff_global(int dtype, int n, int forward, const void* d_input, void* d_output, int batch,
+                        void* stream) {
+  if (batch < 0) return fail(THFF_INVALID_ARGUMENT, "ThunderFFT batch must be nonnegative");
+  if (batch == 0) return THFF_OK;
+  thff_status s = thff_c2c_async(dtype, n, forward, d_input, d_output, batch, stream);
+  if (s != THFF_OK) return s;
+  return thff_sync_check(stream);
+}
+
+}  // extern "C"
