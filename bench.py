@@ -1,0 +1,383 @@
+#!/usr/bin/env python3
+"""Benchmark of the batched C2C FFT hot path.
+
+Workload (one "step"): forward then unnormalized inverse C2C FFT, N = 1024,
+batch 65536 per GPU, float2 storage / TF32 tensor-core arithmetic, separate
+input/output buffers, re/im i.i.d. U[-1,1) from a seed (synthetic: the
+reference publishes no dataset).  Each buffer is 512 MiB, larger than the
+126 MB L2, so every launch streams from HBM.
+
+Metric: HBM throughput of the transform in GB/s (algorithmic bytes: read N*8 +
+write N*8 per transform, twiddles excluded) — the reference's metric is
+"batched C2C FFT us & HBM GB/s (% peak)".  `value` is the whole-job aggregate
+over all ranks (weak scaling: every rank transforms its own 65536 signals;
+the batch dimension shards with no collective on the data path).
+
+Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Under torchrun each rank uses LOCAL_RANK's GPU; rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N = 1024
+BATCH = 65536
+ESZ = 8  # float2
+BYTES_PER_TRANSFORM_BATCH = 2 * N * BATCH * ESZ          # read + write, one direction
+METRIC = "batched C2C FFT HBM GB/s (N=1024, batch 65536/GPU, TF32 fwd+inv)"
+DTYPE = "float"
+
+
+def configure(n: int, batch: int, dtype: str) -> None:
+    """Non-default workloads (profiling / sweeps); the default is config 2."""
+    global N, BATCH, ESZ, BYTES_PER_TRANSFORM_BATCH, METRIC, DTYPE
+    N, BATCH, DTYPE = n, batch, dtype
+    ESZ = 8 if dtype == "float" else 4
+    BYTES_PER_TRANSFORM_BATCH = 2 * N * BATCH * ESZ
+    prec = "TF32" if dtype == "float" else "FP16"
+    METRIC = f"batched C2C FFT HBM GB/s (N={N}, batch {BATCH}/GPU, {prec} fwd+inv)"
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profile_traffic():
+    """dram bytes per launch of the dominant kernel from the committed ncu
+    summary (a line `traffic_bytes_per_launch: <int>`), else None."""
+    p = ROOT / "profiles" / "fft2_f32_n1024_b65536.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(seconds: float = 12.0, sample_batch: int = 2048):
+    """FP64 oracle FFT (fwd + inv) on the host cores over a bounded sample of
+    the same workload; reported in the metric's unit (GB/s of algorithmic
+    bytes).  TEST INFRASTRUCTURE: the oracle is the checker/baseline only."""
+    import oracle
+
+    threads = oracle.hardware_threads()
+    rng = np.random.default_rng(7)
+    x = (rng.uniform(-1, 1, (sample_batch, N)) + 1j * rng.uniform(-1, 1, (sample_batch, N))).astype(np.complex64)
+    oracle.fft_f32io(x[:16], True, threads)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        y = oracle.fft_f32io(x, True, threads)
+        oracle.fft_f32io(y, False, threads)
+        reps += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    bytes_done = reps * 2 * (2 * N * sample_batch * ESZ)
+    return {"value": bytes_done / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x (fwd+inv) of {sample_batch} signals of N={N} (FP64 radix-2, float2 I/O), "
+                      f"{dt:.1f} s on {threads} threads"}
+
+
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference(args):
+    """Reference arm: the reference's CPU path for this workload.  The
+    reference has no host FFT (its checker is cuFFT); the arm times the FP64
+    CPU restatement on all host threads, rank 0 only."""
+    world, rank, _ = dist_setup(args.gpus)
+    if rank != 0:
+        return 0
+    import oracle
+
+    threads = oracle.hardware_threads()
+    sample_batch = 1024
+    rng = np.random.default_rng(7)
+    x = (rng.uniform(-1, 1, (sample_batch, N)) + 1j * rng.uniform(-1, 1, (sample_batch, N))).astype(np.complex64)
+    for _ in range(args.warmup):
+        oracle.fft_f32io(oracle.fft_f32io(x, True, threads), False, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.fft_f32io(oracle.fft_f32io(x, True, threads), False, threads)
+    dt = time.perf_counter() - t0
+    value = args.steps * 2 * (2 * N * sample_batch * ESZ) / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3 * (BATCH / sample_batch),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "C2C fwd+inv, N=1024, batch 65536 per GPU (bounded CPU sample of 1024 signals)",
+                   "n": N, "batch_per_gpu": BATCH, "storage": "float2"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps x (fwd+inv) of {sample_batch} signals, FP64 oracle"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--n", type=int, default=1024, help="transform length (default: config 2)")
+    ap.add_argument("--batch", type=int, default=65536, help="signals per GPU")
+    ap.add_argument("--dtype", default="float", choices=["float", "half"])
+    ap.add_argument("--no-extras", action="store_true", help="skip cuFFT, e2e and CPU legs (profiling)")
+    args = ap.parse_args()
+    configure(args.n, args.batch, args.dtype)
+    if args.no_extras:
+        args.no_cpu_baseline = True
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import thunderfft_b200 as tf
+
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist_mod
+
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        dist = dist_mod
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    if DTYPE == "float":
+        x = torch.complex(torch.rand(BATCH, N, device=dev, generator=g) * 2 - 1,
+                          torch.rand(BATCH, N, device=dev, generator=g) * 2 - 1).contiguous()
+    else:
+        x = (torch.rand(BATCH, N, 2, device=dev, generator=g) - 0.5).half()
+    y = torch.empty_like(x)
+    z = torch.empty_like(x)
+    tf.ThunderFFTInitialize(DTYPE, N)
+
+    def step():
+        tf.c2c_async(DTYPE, N, True, x, y, BATCH, stream)
+        tf.c2c_async(DTYPE, N, False, y, z, BATCH, stream)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    tf.sync_check(stream)
+
+    # correctness gate on a slice of this very run (round trip / N)
+    xs, zs = x[:64].float(), z[:64].float()
+    rt_err = float(((zs / N - xs).abs().pow(2).sum() / xs.abs().pow(2).sum()).sqrt())
+
+    # ---- device-timed region (inputs resident in HBM)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    tf.sync_check(stream)
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    launches = 2 * args.steps
+    total_bytes = world * args.steps * 2 * BYTES_PER_TRANSFORM_BATCH
+    value = total_bytes / (ms_max / 1e3) / 1e9
+    per_launch_us = ms / launches * 1e3
+    achieved = BYTES_PER_TRANSFORM_BATCH / (per_launch_us / 1e6) / 1e9
+
+    # ---- cuFFT on the same GPU / same buffers (extra comparison point)
+    cufft = None
+    if args.no_extras or DTYPE != "float":
+        cufft = None
+    else:
+      try:
+        for _ in range(3):
+            torch.fft.fft(x, out=y)
+        torch.cuda.synchronize(dev)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(10):
+            torch.fft.fft(x, out=y)
+            torch.fft.ifft(y, out=z, norm="forward")
+        c1.record(stream)
+        torch.cuda.synchronize(dev)
+        cms = c0.elapsed_time(c1) / 10
+        cufft = {"value": 2 * BYTES_PER_TRANSFORM_BATCH / (cms / 1e3) / 1e9, "unit": "GB/s",
+                 "ms_per_step": cms, "what": "torch.fft (cuFFT) fp32 C2C fwd+inv, same shapes, 1 GPU"}
+      except Exception as e:  # pragma: no cover
+        cufft = {"error": str(e)}
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if args.no_extras:
+        pass
+    else:
+      try:
+        hx = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+        hx.copy_(x)
+        hz = torch.empty_like(hx, pin_memory=True)
+        dx, dy, dz = torch.empty_like(x), torch.empty_like(x), torch.empty_like(x)
+        e_steps = 3
+
+        def e2e_step():
+            dx.copy_(hx, non_blocking=True)
+            tf.ThunderFFT_global(DTYPE, N, True, dx, dy, BATCH, stream)
+            tf.ThunderFFT_global(DTYPE, N, False, dy, dz, BATCH, stream)
+            hz.copy_(dz, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize(dev)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        et = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        ems = float(et.item())
+        e2e = {"value": world * e_steps * 2 * BYTES_PER_TRANSFORM_BATCH / (ems / 1e3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": int(hx.numel() * hx.element_size()),
+               "d2h_bytes_per_step": int(hz.numel() * hz.element_size()),
+               "ms_per_step": ems / e_steps}
+      except Exception as e:  # pragma: no cover
+        e2e = {"error": str(e)}
+
+    peak, peak_kind = measured_peaks()
+    line = None
+    if rank == 0:
+        cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline()
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "tf32" if DTYPE == "float" else "f16",
+            "data": "synthetic",
+            "config": {"workload": (f"C2C fwd+inv (BASELINE config 2), N={N}, batch {BATCH} per GPU, float2"
+                                    if DTYPE == "float" else f"C2C fwd+inv FP16, N={N}, batch {BATCH} per GPU"),
+                       "n": N, "batch_per_gpu": BATCH, "storage": "float2" if DTYPE == "float" else "half2",
+                       "parallelism": f"batch-shard x{world}, no collective",
+                       "l2": (f"inputs {N * BATCH * ESZ >> 20} MiB per buffer > 126 MB L2 (no flush needed)"
+                              if N * BATCH * ESZ > 126e6 else "WARNING: buffers fit in L2")},
+            "us_per_transform_batch": per_launch_us,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": profile_traffic(),
+                         "kernel": (f"thff::fft2_kernel<Fft2Cfg<{str(DTYPE == 'half').lower()},{N}>>" if N > 64
+                                    else f"thff::dft1_kernel<Dft1Cfg<{str(DTYPE == 'half').lower()}>>"),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6650 GB/s"},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+            "cufft": cufft,
+            "roundtrip_rel_l2": rt_err,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -279,7 +279,7 @@ thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* 
   const bool use_tma = aligned16(in);
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
-  {
+  if (use_tma) {
     const uint64_t sig_bytes = uint64_t(C::N) * 2 * C::ESZ;
     uint64_t dims[5], strides[4];
     uint32_t box[5];
