@@ -1,0 +1,107 @@
+// thunderfft_impl_helper.cuh — layout-aware data movement of the device API.
+//
+// Fragment convention of this library: with P = 32 * warp_per_block<N>
+// threads and t = threadIdx.x + 32 * threadIdx.y, thread t holds element
+// e = t + P * i (i < 32) of the block's tile in signal order (e = j*N + n).
+// The input fragment holds input elements, the output fragment output
+// elements, both in natural order; the helpers translate to and from any
+// layout_t (strides, periodic padding, digit-reversed shared tiles).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "util_arith.h"
+#include "util_cuda.h"
+
+namespace thunderfft {
+namespace detail {
+
+template <typename sL>
+__device__ __forceinline__ int layout_index(int j, int n) {
+  int idx = n * sL::elem_stride + j * sL::batch_stride;
+  return idx + (idx / sL::pad_period) * sL::pad;
+}
+
+// Position in a layout's tile that holds natural element n of a signal.
+template <typename sL>
+__device__ __forceinline__ int stored_position(int n) {
+  if constexpr (sL::reversed) return unreverse_bit_groups<2, LOG2P_builtin<sL::N>>(n);
+  else return n;
+}
+
+template <int N, int batch>
+struct frag {
+  static constexpr int P = 32 * warp_per_block<N>;
+  static constexpr int EPT = N * batch / P;
+  static_assert(EPT * P == N * batch, "tile must split evenly over the block");
+};
+
+__device__ __forceinline__ int block_thread() { return threadIdx.x + threadIdx.y * blockDim.x; }
+
+}  // namespace detail
+
+// Contiguous natural-order global tile -> shared memory described by sL
+// (sL::reversed stores the digit-reversed permutation).
+template <typename T, typename sL>
+__device__ __forceinline__ void ThunderFFT_gmem2smem(vec2_t<T>* __restrict__ smem, const vec2_t<T>* __restrict__ gmem) {
+  constexpr int N = sL::N, B = sL::batch, P = 32 * warp_per_block<N>;
+  const int t = detail::block_thread();
+  for (int e = t; e < N * B; e += P) {
+    const int j = e / N, p = e % N;
+    const int n = sL::reversed ? reverse_bit_groups<2, LOG2P_builtin<N>>(p) : p;
+    smem[detail::layout_index<sL>(j, p)] = gmem[j * N + n];
+  }
+}
+
+// Shared memory described by sL -> contiguous natural-order global tile.
+// Requires sL::reversed == false (a reversed layout writes nothing).
+template <typename T, typename sL>
+__device__ __forceinline__ void ThunderFFT_smem2gmem(vec2_t<T>* __restrict__ gmem, const vec2_t<T>* __restrict__ smem) {
+  constexpr int N = sL::N, B = sL::batch, P = 32 * warp_per_block<N>;
+  if constexpr (!sL::reversed) {
+    const int t = detail::block_thread();
+    for (int e = t; e < N * B; e += P) gmem[e] = smem[detail::layout_index<sL>(e / N, e % N)];
+  }
+}
+
+// Shared memory described by sL -> input fragment.
+template <typename T, typename sL>
+__device__ __forceinline__ void ThunderFFT_smem2reg(vec2_t<T>* __restrict__ reg, const vec2_t<T>* __restrict__ smem) {
+  using F = detail::frag<sL::N, sL::batch>;
+  const int t = detail::block_thread();
+#pragma unroll
+  for (int i = 0; i < F::EPT; ++i) {
+    const int e = t + F::P * i;
+    const int j = e / sL::N, n = e % sL::N;
+    reg[i] = smem[detail::layout_index<sL>(j, detail::stored_position<sL>(n))];
+  }
+}
+
+// Output fragment -> shared memory described by sL (natural order, or the
+// digit-reversed order when sL::reversed).
+template <typename T, typename sL>
+__device__ __forceinline__ void ThunderFFT_reg2smem(vec2_t<T>* __restrict__ smem, const vec2_t<T>* __restrict__ reg) {
+  using F = detail::frag<sL::N, sL::batch>;
+  const int t = detail::block_thread();
+#pragma unroll
+  for (int i = 0; i < F::EPT; ++i) {
+    const int e = t + F::P * i;
+    const int j = e / sL::N, k = e % sL::N;
+    smem[detail::layout_index<sL>(j, detail::stored_position<sL>(k))] = reg[i];
+  }
+}
+
+// Global memory -> input fragment (gmem = block-local base of `batch`
+// contiguous natural-order signals).
+template <typename T, int N, int batch>
+__device__ __forceinline__ void ThunderFFT_gmem2reg(vec2_t<T>* __restrict__ reg, const vec2_t<T>* __restrict__ gmem) {
+  ThunderFFT_smem2reg<T, layout_t<N, batch, 1, N, 1, 0, false>>(reg, gmem);
+}
+
+// Output fragment -> natural-order contiguous global tile.
+template <typename T, int N, int batch>
+__device__ __forceinline__ void ThunderFFT_reg2gmem(vec2_t<T>* __restrict__ gmem, const vec2_t<T>* __restrict__ reg) {
+  ThunderFFT_reg2smem<T, layout_t<N, batch, 1, N, 1, 0, false>>(gmem, reg);
+}
+
+}  // namespace thunderfft

@@ -70,7 +70,7 @@ class _DevicePtr:
     """Wrap a raw device pointer for torch.as_tensor (read-only view)."""
 
     def __init__(self, ptr: int, nbytes: int):
-        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, True),
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
                                          "version": 3}
 
 

@@ -1,0 +1,52 @@
+"""The C++ header API used the way a reference user uses it
+(include/thunderfft/thunderfft.cuh compiled into a user program and linked
+with libthunderfft_b200.so): host contract (no GPU), device-API composition
+and twiddle-cache lifecycle (GPU)."""
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE / "cpp"))
+import build as cppbuild  # noqa: E402
+
+
+def test_host_contract_program_without_gpu():
+    exe = cppbuild.build("host_contract")
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120,
+                         env={"CUDA_VISIBLE_DEVICES": "", "PATH": "/usr/bin:/bin"})
+    assert res.returncode == 0, res.stderr
+    assert "18 checks passed" in res.stdout
+
+
+@pytest.mark.gpu
+def test_device_api_composition(cuda, tmp_path):
+    exe = cppbuild.build("device_api")
+    res = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout + res.stderr
+    files = sorted(tmp_path.glob("devapi_*.bin"))
+    assert len(files) == 28
+    for f in files:
+        raw = f.read_bytes()
+        n, batch, guard_bad, _ = np.frombuffer(raw[:16], dtype=np.int32)
+        data = np.frombuffer(raw[16:], dtype=np.complex64).reshape(3, batch, n)
+        x, y, y2 = data.astype(np.complex128)
+        forward = f.stem.endswith("fwd")
+        ref = oracle.fft(x, forward)
+        assert guard_bad == 0, f.name
+        assert np.isfinite(y).all() and np.isfinite(y2).all(), f.name
+        e1, e2 = oracle.rel_l2(y, ref), oracle.rel_l2(y2, ref)
+        assert e1 <= 5e-3 and e2 <= 5e-3, (f.name, e1, e2)
+
+
+@pytest.mark.gpu
+def test_cache_lifecycle_program(cuda):
+    exe = cppbuild.build("cache_lifecycle")
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "checks passed" in res.stdout
