@@ -166,3 +166,41 @@ def rel_linf(got: np.ndarray, ref: np.ndarray) -> float:
     m = np.max(np.abs(ref))
     e = np.max(np.abs(got - ref))
     return float(e / m) if m > 0 else float(e)
+
+
+# ---------------------------------------------------------------------------
+# The reference's own GPU implementation (oracle/_ref/libthff_ref.so, built by
+# oracle/build_ref.py from the reference headers).  TEST INFRASTRUCTURE: used
+# only to compare outputs and to time the reference beside this library.
+# ---------------------------------------------------------------------------
+REF_LIB = HERE / "_ref" / "libthff_ref.so"
+_ref = None
+
+
+def ref_available() -> bool:
+    return REF_LIB.exists()
+
+
+def ref_lib():
+    global _ref
+    if _ref is None:
+        L = ctypes.CDLL(str(REF_LIB))
+        vp, i32 = ctypes.c_void_p, ctypes.c_int
+        L.thff_ref_initialize.argtypes = [i32, i32]
+        L.thff_ref_finalize.argtypes = [i32]
+        L.thff_ref_global.argtypes = [i32, i32, i32, vp, vp, i32, vp]
+        L.thff_ref_last_error.restype = ctypes.c_char_p
+        for n in ("thff_ref_initialize", "thff_ref_finalize", "thff_ref_global"):
+            getattr(L, n).restype = i32
+        _ref = L
+    return _ref
+
+
+def ref_global(dtype: str, n: int, forward: bool, d_in: int, d_out: int, batch: int, stream: int = 0) -> None:
+    """Run the reference's ThunderFFT_global<T,N,forward> (synchronizes)."""
+    L = ref_lib()
+    code = 0 if dtype == "float" else 1
+    if L.thff_ref_initialize(code, n) != 0:
+        raise RuntimeError(L.thff_ref_last_error().decode())
+    if L.thff_ref_global(code, n, 1 if forward else 0, d_in, d_out, batch, stream) != 0:
+        raise RuntimeError(L.thff_ref_last_error().decode())
