@@ -74,6 +74,34 @@ thff_status thff_c2c_async(int dtype, int n, int forward, const void* d_input, v
  * launches on this device. */
 thff_status thff_sync_check(void* stream);
 
+
+/* ---- fused real 1-D FFT convolution --------------------------------------
+ * Counterpart of the reference's fused conv1d sample
+ * (sample/conv1d/conv1d_fullfft_l4096_thunder.cu:280-331), here for float
+ * storage with TF32 tensor-core arithmetic.  For each of `batch` real
+ * signals x[b] of length `lin` (zero-padded to n) and one real filter h:
+ *     y[b][m] = (1/n) * sum_k x[b][(m-k) mod n] * h[k],   m < n,
+ * computed as FFT -> multiply by the filter spectrum -> inverse FFT in ONE
+ * kernel.  n in {1024, 4096}; lin <= n and a multiple of sqrt(n); x must be
+ * 16-byte aligned; y holds batch*n floats.  With lin + taps - 1 <= n the
+ * result equals the linear convolution. */
+
+/* Bytes of the filter spectrum buffer (complex fp32, n entries). */
+long long thff_conv1d_spectrum_bytes(int dtype, int n);
+
+/* spectrum[k] = (1/n) * sum_{j<taps} h[j] exp(-2 pi i j k / n), computed on
+ * the device (the reference prepares it with cuFFT). */
+thff_status thff_conv1d_filter_spectrum(int dtype, int n, const float* d_filter, int taps, void* d_spectrum,
+                                        void* stream);
+
+/* Asynchronous fused convolution (see above). */
+thff_status thff_conv1d_async(int dtype, int n, int lin, const void* d_x, const void* d_spectrum, void* d_y,
+                              long long batch, void* stream);
+
+/* Same, then synchronizes `stream` and reports device-side errors. */
+thff_status thff_conv1d(int dtype, int n, int lin, const void* d_x, const void* d_spectrum, void* d_y,
+                        long long batch, void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

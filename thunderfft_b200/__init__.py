@@ -33,7 +33,7 @@ from typing import Optional
 __all__ = [
     "ThunderFFTInitialize", "ThunderFFTFinalize", "ThunderFFT_global", "c2c_async", "sync_check",
     "twiddle_table", "fft", "load_library", "library_path", "SUPPORTED_N", "batch_per_block",
-    "warp_per_block", "threads_per_warp", "version",
+    "warp_per_block", "threads_per_warp", "version", "conv1d_filter_spectrum", "conv1d",
 ]
 
 SUPPORTED_N = (64, 128, 256, 512, 1024, 2048, 4096)
@@ -74,8 +74,14 @@ def load_library() -> ctypes.CDLL:
     lib.thff_global.argtypes = [i32, i32, i32, vp, vp, i32, vp]
     lib.thff_c2c_async.argtypes = [i32, i32, i32, vp, vp, i64, vp]
     lib.thff_sync_check.argtypes = [vp]
+    lib.thff_conv1d_spectrum_bytes.argtypes = [i32, i32]
+    lib.thff_conv1d_spectrum_bytes.restype = i64
+    lib.thff_conv1d_filter_spectrum.argtypes = [i32, i32, vp, i32, vp, vp]
+    lib.thff_conv1d_async.argtypes = [i32, i32, i32, vp, vp, vp, i64, vp]
+    lib.thff_conv1d.argtypes = [i32, i32, i32, vp, vp, vp, i64, vp]
     for name in ("thff_initialize", "thff_finalize", "thff_twiddle_table", "thff_global",
-                 "thff_c2c_async", "thff_sync_check"):
+                 "thff_c2c_async", "thff_sync_check", "thff_conv1d_filter_spectrum", "thff_conv1d_async",
+                 "thff_conv1d"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -191,4 +197,37 @@ def fft(x, forward: bool = True, out=None, stream=None, sync: bool = True):
     c2c_async(T, n, forward, x, out, batch, stream if stream is not None else torch.cuda.current_stream())
     if sync:
         sync_check(stream if stream is not None else torch.cuda.current_stream())
+    return out
+
+
+def conv1d_filter_spectrum(h, n: int, stream=None):
+    """Filter spectrum for `conv1d`: H[k] = (1/n) sum_j h[j] exp(-2 pi i j k / n)
+    for a real float32 CUDA tensor h (taps <= n); returns a complex64 tensor."""
+    import torch
+
+    if not (h.is_cuda and h.dtype == torch.float32 and h.dim() == 1 and h.is_contiguous()):
+        raise ValueError("filter must be a contiguous 1-D float32 CUDA tensor")
+    spec = torch.empty(n, dtype=torch.complex64, device=h.device)
+    st = stream if stream is not None else torch.cuda.current_stream(h.device)
+    _check(load_library().thff_conv1d_filter_spectrum(0, int(n), h.data_ptr(), int(h.numel()), spec.data_ptr(),
+                                                      _stream_handle(st)))
+    return spec
+
+
+def conv1d(x, spectrum, n: int, out=None, stream=None, sync: bool = True):
+    """Fused real circular convolution of every row of x (float32 CUDA tensor
+    [batch, lin], zero-padded to n) with the filter whose spectrum is given:
+    out[b, m] = (1/n) sum_k x[b][(m-k) mod n] h[k] (one kernel: FFT, multiply,
+    inverse FFT).  Returns out [batch, n] float32."""
+    import torch
+
+    if not (x.is_cuda and x.dtype == torch.float32 and x.dim() == 2 and x.is_contiguous()):
+        raise ValueError("x must be a contiguous [batch, lin] float32 CUDA tensor")
+    batch, lin = x.shape
+    if out is None:
+        out = torch.empty(batch, n, dtype=torch.float32, device=x.device)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    fn = load_library().thff_conv1d if sync else load_library().thff_conv1d_async
+    _check(fn(0, int(n), int(lin), x.data_ptr(), spectrum.data_ptr(), out.data_ptr(), int(batch),
+              _stream_handle(st)))
     return out

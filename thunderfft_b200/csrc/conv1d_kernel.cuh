@@ -1,0 +1,323 @@
+// conv1d_kernel.cuh — fused real 1-D FFT convolution on sm_100a.
+//
+// Counterpart of the reference's fused conv1d sample kernel
+// (sample/conv1d/conv1d_fullfft_l4096_thunder.cu:280-331: real input ->
+// FFT -> x filter spectrum -> inverse FFT -> real output in one kernel).
+// For each real signal x (length Lin <= N, zero-padded to N) and one real
+// filter with spectrum H (1/N folded in):
+//     y = IFFT( FFT(x) * H ),   i.e.  y[m] = (1/N) sum_k x[(m-k) mod N] h[k].
+//
+// Two real signals share one complex transform: z = x0 + i*x1 gives
+// IFFT(FFT(z) * H) = (x0 (*) h) + i (x1 (*) h) because h is real, so the real
+// and imaginary parts of the result are the two outputs.
+//
+// N = L * L runs as four tcgen05 stages on one tile (TC complex signals):
+//   S1 forward DFT over s     (B1: input rows, TMA, zero rows for padding)
+//   E1 combine + twiddle w_N^-(a ks)           -> B2
+//   S2 forward DFT over a, E2 combine, * H      -> B3 (transposed = inverse input order)
+//   S3 inverse DFT over s', E3 combine + w_N^+(a ks) -> B4
+//   S4 inverse DFT over a', E4 combine          -> y (global)
+// Every B operand is planar: columns (signal c, plane re|im, index) so that
+// one TMEM 16x256b load gives a thread, for two neighbouring indices, all
+// four partial sums (cos|sin) x (re|im) of its outputs.  All stages use the
+// same forward DFT matrix; the inverse stages flip the sine terms in the
+// epilogue.  The MMA thread runs the four stages of four different tiles in
+// each round (S1(r), S2(r-1), S3(r-2), S4(r-3)) so all stages overlap.
+#pragma once
+#include "fft_kernels.cuh"
+
+namespace thff {
+
+template <int kN>
+struct Conv1dCfg {
+  using D = DType<false>;  // float storage / TF32 tensor cores
+  static constexpr int N = kN;
+  static constexpr int L = (kN == 4096) ? 64 : 32;     // N = L * L
+  static_assert(L * L == N, "conv1d supports N = 1024 and 4096");
+  static constexpr int M = 2 * L;                        // MMA M (rows: ks x {cos, sin})
+  static constexpr int TC = (kN == 4096) ? 1 : 4;        // complex signals (= 2*TC real) per tile
+  static constexpr int NCOL = TC * 2 * L;                // MMA N (columns: c x plane x index)
+  static constexpr int E = 32;                           // floats per 128-B atom row
+  static constexpr int H = L * 4 / 128;                  // 128-B atoms per input row
+  static constexpr int TILE_BYTES = TC * N * 8;          // planar complex tile (B1..B4)
+  static constexpr int A_BYTES = M * L * 4;
+  static constexpr uint32_t LBO = L * 128;
+  static constexpr int KSTEPS = L / 8;
+  static constexpr int SIN = (kN == 4096) ? 2 : 3;
+  static constexpr uint32_t OFF_A = 0;
+  static constexpr uint32_t OFF_IN = (A_BYTES + 1023) / 1024 * 1024;
+  static constexpr uint32_t OFF_B = OFF_IN + SIN * TILE_BYTES;   // B2, B3, B4
+  static constexpr uint32_t SMEM_BYTES = OFF_B + 3 * TILE_BYTES + 1024;
+  static_assert(SMEM_BYTES + 1024 <= 232448, "shared memory budget");
+  static_assert(M == 128 ? NCOL <= 128 : NCOL <= 256, "TMEM budget (4 accumulators)");
+  static constexpr int kThreads = 320;
+  static constexpr int kBlocks = M / 64;                 // 16-row blocks per epilogue warp
+};
+
+struct Conv1dParams {
+  const float* x;        // [batch][lin] real input
+  float* y;              // [batch][N] real output
+  const void* a;         // forward DFT matrix image (K-major, no swizzle)
+  const float2* tw;      // forward twiddles exp(-2 pi i k / N)
+  const float2* spec;    // filter spectrum H[k] / N (complex fp32)
+  long long batch;       // real signals
+  int lin;               // input length (<= N, multiple of L)
+  int rows_valid;        // lin / L: non-zero K rows of stage 1
+  uint32_t* err;
+};
+
+namespace detail {
+
+template <class C>
+__device__ __forceinline__ uint32_t planar_off(int krow, int col) {
+  return (uint32_t)(col / C::E) * C::LBO + C::D::swz((uint32_t)krow * 128u + (uint32_t)(col % C::E) * 4u);
+}
+
+// TMEM address of accumulator s (0..3) for 16-row block `block` of this warp.
+template <class C>
+__device__ __forceinline__ uint32_t acc_addr(uint32_t tmem, int s, uint32_t q, int bi) {
+  if constexpr (C::M == 64) {
+    return tmem + ((32u * q + 16u * (uint32_t)(s & 1)) << 16) + 256u * (uint32_t)(s >> 1);
+  } else {
+    return tmem + ((32u * q + 16u * (uint32_t)bi) << 16) + 128u * (uint32_t)s;
+  }
+}
+
+// Load the 2L planar columns of complex signal c (re plane then im plane).
+template <class C>
+__device__ __forceinline__ void load_planar(uint32_t addr, int c, uint32_t (&re)[C::L / 2], uint32_t (&im)[C::L / 2]);
+
+}  // namespace detail
+
+template <class C>
+__global__ void __launch_bounds__(C::kThreads, 1)
+conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) {
+  using namespace sm100;
+  using D = typename C::D;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN];
+  __shared__ uint64_t bar_d_full[4], bar_d_empty[4], bar_b_full[3], bar_b_empty[3], bar_const, bar_done;
+  __shared__ uint32_t tmem_slot;
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const long long batch = p.batch;
+  const long long per_tile = 2LL * C::TC;
+  const long long num_tiles = (batch + per_tile - 1) / per_tile;
+  const int T = (int)((num_tiles > blockIdx.x) ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::SIN; ++i) { mbar_init(&bar_in_full[i], 1); mbar_init(&bar_in_empty[i], 1); }
+    for (int i = 0; i < 4; ++i) { mbar_init(&bar_d_full[i], 1); mbar_init(&bar_d_empty[i], 4); }
+    for (int i = 0; i < 3; ++i) { mbar_init(&bar_b_full[i], 4); mbar_init(&bar_b_empty[i], 1); }
+    mbar_init(&bar_const, 1);
+    mbar_init(&bar_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) { tmem_alloc(&tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  uint8_t* const bbuf = smem + C::OFF_B;  // B2, B3, B4
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_x);
+      mbar_arrive_expect_tx(&bar_const, C::A_BYTES);
+      bulk_load(smem + C::OFF_A, p.a, C::A_BYTES, &bar_const);
+    }
+    for (int i = 0; i < T; ++i) {
+      const long long tile = blockIdx.x + (long long)i * gridDim.x;
+      const int slot = i % C::SIN;
+      if (!mbar_wait_warp(&bar_in_empty[slot], ((uint32_t)(i / C::SIN) & 1u) ^ 1u, p.err, kDevTimeoutProducer)) break;
+      if (lane == 0) {
+        // 2*TC real signals, rows s < L (rows >= lin/L and signals >= batch
+        // are zero-filled by the tensor map bounds)
+        mbar_arrive_expect_tx(&bar_in_full[slot], C::TILE_BYTES);
+        tma_load_4d(smem + C::OFF_IN + slot * C::TILE_BYTES, &tmap_x, &bar_in_full[slot], 0, 0, 0,
+                    (int)(tile * per_tile));
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar_const, 0, p.err, kDevTimeoutMma);
+      const uint32_t a = smem_u32(smem + C::OFF_A);
+      const uint32_t idesc = instr_desc(D::kFmt, C::M, C::NCOL, 0, 1);
+      const uint32_t lboA = (C::M / 8) * 128;
+      const int ks1 = (p.rows_valid + 7) / 8;  // stage 1 skips all-zero K rows
+      auto stage = [&](uint32_t d, uint32_t b, int ksteps) {
+#pragma unroll 1
+        for (int k = 0; k < ksteps; ++k) {
+          const uint64_t ad = smem_desc(a + k * 2 * lboA, lboA, 128, kSwNone);
+          const uint64_t bd = smem_desc(b + k * 1024u, C::LBO, D::kBSbo, D::kBSwizzle);
+          umma_tf32(d, ad, bd, idesc, k > 0);
+        }
+      };
+      for (int r = 0; ok && r < T + 3; ++r) {
+        // S1(r): input slot -> D0
+        if (r < T) {
+          const int slot = r % C::SIN;
+          if (!mbar_wait(&bar_in_full[slot], (uint32_t)(r / C::SIN) & 1u, p.err, kDevTimeoutMma) ||
+              !mbar_wait(&bar_d_empty[0], ((uint32_t)r & 1u) ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          stage(detail::acc_addr<C>(tmem, 0, 0, 0), smem_u32(smem + C::OFF_IN + slot * C::TILE_BYTES), ks1);
+          umma_commit(&bar_in_empty[slot]);
+          umma_commit(&bar_d_full[0]);
+        }
+        // S2(r-1), S3(r-2), S4(r-3): B(s-2) -> D(s-1)
+#pragma unroll 1
+        for (int s = 1; s < 4; ++s) {
+          const int j = r - s;
+          if (j < 0 || j >= T) continue;
+          if (!mbar_wait(&bar_b_full[s - 1], (uint32_t)j & 1u, p.err, kDevTimeoutMma) ||
+              !mbar_wait(&bar_d_empty[s], ((uint32_t)j & 1u) ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          stage(detail::acc_addr<C>(tmem, s, 0, 0), smem_u32(bbuf + (s - 1) * C::TILE_BYTES), C::KSTEPS);
+          umma_commit(&bar_b_empty[s - 1]);
+          umma_commit(&bar_d_full[s]);
+        }
+      }
+      umma_commit(&bar_done);
+      mbar_wait(&bar_done, 0, p.err, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogues
+    // group A (warps 2-5): E1 (D0 -> B2) and E3 (D2 -> B4)
+    // group B (warps 6-9): E2 (D1 -> *H -> B3) and E4 (D3 -> y)
+    const bool groupA = warp < 6;
+    const uint32_t q = warp & 3u;
+    const int l4 = (int)(lane & 3u);
+    // Each thread owns index pairs (i0, i0+1), i0 = 8u + 2*l4, u < L/8, of
+    // row pair ks = block*8 + lane/4.  Group A keeps the forward twiddles
+    // w_N^-(a ks) of its pairs in registers (inverse = conjugate).
+    constexpr int kU = C::L / 8;
+    float2 tw[C::kBlocks][kU][2];
+#pragma unroll
+    for (int bi = 0; bi < C::kBlocks; ++bi) {
+      const int ks = (C::M == 64 ? (int)q : (int)(2 * q + bi)) * 8 + (int)(lane >> 2);
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+#pragma unroll
+        for (int o = 0; o < 2; ++o) tw[bi][u][o] = groupA ? p.tw[((8 * u + 2 * l4 + o) * ks) % C::N] : make_float2(0.f, 0.f);
+    }
+    const int first = groupA ? 0 : 1;      // E1/E3 or E2/E4
+    for (int r = 0; r < T + 3; ++r) {
+      bool ok = true;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        const int s = first + 2 * which;   // accumulator index 0..3
+        const int j = r - s;               // tile of this stage in round r
+        if (j < 0 || j >= T) continue;
+        const uint32_t ph = (uint32_t)j & 1u;
+        if (!mbar_wait_warp(&bar_d_full[s], ph, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+        if (s < 3 && !mbar_wait_warp(&bar_b_empty[s], ph ^ 1u, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+        tc_fence_after();
+        const bool inverse = s >= 2;
+        const long long tile = blockIdx.x + (long long)j * gridDim.x;
+        const uint32_t bdst = smem_u32(bbuf + (s < 3 ? s : 0) * C::TILE_BYTES);
+#pragma unroll
+        for (int bi = 0; bi < C::kBlocks; ++bi) {
+          const int blk = (C::M == 64) ? (int)q : (int)(2 * q + bi);
+          const int ks = blk * 8 + (int)(lane >> 2);  // row pair: stage output index
+          const uint32_t abase = detail::acc_addr<C>(tmem, s, q, bi);
+#pragma unroll 1
+          for (int c = 0; c < C::TC; ++c) {
+            // planar columns of signal c: re plane [c*2L, c*2L+L), im plane [c*2L+L, c*2L+2L)
+            uint32_t vr[C::L / 2], vi[C::L / 2];
+            if constexpr (C::L == 64) {
+              uint32_t t0[32], t1[32];
+              tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L), t0);
+              tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L + C::L), t1);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) { vr[i] = t0[i]; vi[i] = t1[i]; }
+            } else {
+              uint32_t t0[32];
+              tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L), t0);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) { vr[i] = t0[i]; vi[i] = t0[16 + i]; }
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+              float yr[2], yi[2];
+#pragma unroll
+              for (int o = 0; o < 2; ++o) {
+                const float RR = __uint_as_float(vr[4 * u + o]), IR = __uint_as_float(vr[4 * u + 2 + o]);
+                const float RI = __uint_as_float(vi[4 * u + o]), II = __uint_as_float(vi[4 * u + 2 + o]);
+                yr[o] = inverse ? RR + II : RR - II;
+                yi[o] = inverse ? RI - IR : IR + RI;
+              }
+              const int i0 = 8 * u + 2 * l4;  // input index pair of this stage
+              if (s == 0 || s == 2) {
+                // twiddle, then B(s+2)[K row = i][c, plane, ks]
+#pragma unroll
+                for (int o = 0; o < 2; ++o) {
+                  const float2 w = tw[bi][u][o];
+                  const float wy = inverse ? -w.y : w.y;
+                  const float zr = yr[o] * w.x - yi[o] * wy, zi = yr[o] * wy + yi[o] * w.x;
+                  st_shared_b32(bdst + detail::planar_off<C>(i0 + o, c * 2 * C::L + ks), __float_as_uint(round_tf32(zr)));
+                  st_shared_b32(bdst + detail::planar_off<C>(i0 + o, c * 2 * C::L + C::L + ks), __float_as_uint(round_tf32(zi)));
+                }
+              } else if (s == 1) {
+                // X[k], k = L*ks + i (ks = ka here): multiply by H, write the
+                // inverse's input B3[K row = ks][c, plane, i]
+                const float4 h = __ldg(reinterpret_cast<const float4*>(p.spec + C::L * ks + i0));
+                const float z0r = yr[0] * h.x - yi[0] * h.y, z0i = yr[0] * h.y + yi[0] * h.x;
+                const float z1r = yr[1] * h.z - yi[1] * h.w, z1i = yr[1] * h.w + yi[1] * h.z;
+                st_shared_v2(bdst + detail::planar_off<C>(ks, c * 2 * C::L + i0), round_tf32(z0r), round_tf32(z1r));
+                st_shared_v2(bdst + detail::planar_off<C>(ks, c * 2 * C::L + C::L + i0), round_tf32(z0i), round_tf32(z1i));
+              } else {
+                // output m = L*ks + i: re -> signal 2c, im -> signal 2c+1
+                const long long sig0 = tile * (2LL * C::TC) + 2 * c;
+                const long long m = (long long)C::L * ks + i0;
+                if (sig0 < batch)
+                  *reinterpret_cast<float2*>(p.y + sig0 * C::N + m) = make_float2(yr[0], yr[1]);
+                if (sig0 + 1 < batch)
+                  *reinterpret_cast<float2*>(p.y + (sig0 + 1) * C::N + m) = make_float2(yi[0], yi[1]);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        if (s < 3) fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bar_d_empty[s]);
+          if (s < 3) mbar_arrive(&bar_b_full[s]);
+        }
+      }
+      if (!ok) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Filter spectrum H[k] = (1/N) sum_{j<taps} h[j] exp(-2 pi i j k / N) by
+// direct summation with exact angle reduction (one thread per bin).
+__global__ void conv1d_spectrum_kernel(const float* __restrict__ h, int taps, int n, float2* __restrict__ spec) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  double sr = 0.0, si = 0.0;
+  for (int j = 0; j < taps; ++j) {
+    const long long idx = ((long long)j * k) % n;
+    double s, c;
+    sincospi(-2.0 * (double)idx / (double)n, &s, &c);
+    sr += h[j] * c;
+    si += h[j] * s;
+  }
+  spec[k] = make_float2((float)(sr / n), (float)(si / n));
+}
+
+}  // namespace thff

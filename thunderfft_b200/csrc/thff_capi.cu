@@ -21,6 +21,7 @@
 
 #include "../../include/thff.h"
 #include "fft_kernels.cuh"
+#include "conv1d_kernel.cuh"
 
 namespace {
 
@@ -351,6 +352,60 @@ thff_status dispatch_c2c(DeviceState& st, const Consts& c, int dtype, int n, con
   return fail(THFF_INVALID_ARGUMENT, "[ThunderFFT] unsupported FFT length");
 }
 
+template <int kN>
+thff_status launch_conv1d(DeviceState& st, const Consts& c, int lin, const void* x, const void* spec, void* y,
+                          long long batch, cudaStream_t stream) {
+  using C = thff::Conv1dCfg<kN>;
+  CUtensorMap map;
+  std::memset(&map, 0, sizeof(map));
+  const uint64_t dims[4] = {uint64_t(C::E), uint64_t(lin / C::L), uint64_t(C::H), uint64_t(batch)};
+  const uint64_t strides[3] = {uint64_t(C::L) * 4, 128, uint64_t(lin) * 4};
+  const uint32_t box[4] = {uint32_t(C::E), uint32_t(C::L), uint32_t(C::H), uint32_t(2 * C::TC)};
+  thff_status s = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, x, dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  if (s != THFF_OK) return s;
+  thff::Conv1dParams p;
+  p.x = static_cast<const float*>(x);
+  p.y = static_cast<float*>(y);
+  p.a = c.a1;
+  p.tw = reinterpret_cast<const float2*>(c.tw);
+  p.spec = static_cast<const float2*>(spec);
+  p.batch = batch;
+  p.lin = lin;
+  p.rows_valid = lin / C::L;
+  p.err = st.d_err;
+  auto kernel = thff::conv1d_kernel<C>;
+  if ((s = set_smem_attr(st, kernel, int(C::SMEM_BYTES))) != THFF_OK) return s;
+  const long long tiles = (batch + 2 * C::TC - 1) / (2 * C::TC);
+  const long long grid = tiles < st.sms ? tiles : st.sms;
+  kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map, p);
+  THFF_CUDA(cudaGetLastError(), "conv1d launch");
+  return THFF_OK;
+}
+
+// Stage matrix + twiddles of the conv kernel: the forward DFT matrix of
+// length L = sqrt(n) (one group) and the forward twiddles of length n.
+thff_status get_conv_consts(DeviceState& st, int n, const Consts** out) {
+  const int key = 7 * 8192 + n;
+  auto it = st.consts.find(key);
+  if (it == st.consts.end()) {
+    Consts c;
+    const int L = n == 4096 ? 64 : 32;
+    thff_status s = upload(build_stage_matrix(L, 1, -1, false), &c.a1);
+    if (s != THFF_OK) return s;
+    std::vector<uint8_t> tw(size_t(n) * 8);
+    for (int k = 0; k < n; ++k) {
+      const double th = -kTau * double(k) / double(n);
+      const float v[2] = {float(std::cos(th)), float(std::sin(th))};
+      std::memcpy(tw.data() + size_t(k) * 8, v, 8);
+    }
+    if ((s = upload(tw, &c.tw)) != THFF_OK) return s;
+    it = st.consts.emplace(key, c).first;
+  }
+  *out = &it->second;
+  return THFF_OK;
+}
+
 thff_status read_device_error(DeviceState& st, cudaStream_t stream) {
   if (!t_err_host) THFF_CUDA(cudaMallocHost(&t_err_host, sizeof(uint32_t)), "cudaMallocHost(error word)");
   *t_err_host = 0;
@@ -491,6 +546,57 @@ thff_status thff_global(int dtype, int n, int forward, const void* d_input, void
   if (batch == 0) return THFF_OK;
   thff_status s = thff_c2c_async(dtype, n, forward, d_input, d_output, batch, stream);
   if (s != THFF_OK) return s;
+  return thff_sync_check(stream);
+}
+
+long long thff_conv1d_spectrum_bytes(int dtype, int n) {
+  if (dtype != THFF_F32 || (n != 1024 && n != 4096)) return -1;
+  return (long long)n * 8;
+}
+
+thff_status thff_conv1d_filter_spectrum(int dtype, int n, const float* d_filter, int taps, void* d_spectrum,
+                                        void* stream) {
+  if (dtype != THFF_F32) return fail(THFF_INVALID_ARGUMENT, "conv1d: float storage only");
+  if (n != 1024 && n != 4096) return fail(THFF_INVALID_ARGUMENT, "conv1d: n must be 1024 or 4096");
+  if (taps < 1 || taps > n) return fail(THFF_INVALID_ARGUMENT, "conv1d: taps must be in [1, n]");
+  if (!d_filter || !d_spectrum) return fail(THFF_INVALID_ARGUMENT, "conv1d: null filter or spectrum");
+  thff::conv1d_spectrum_kernel<<<(n + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      d_filter, taps, n, static_cast<float2*>(d_spectrum));
+  THFF_CUDA(cudaGetLastError(), "conv1d spectrum launch");
+  return THFF_OK;
+}
+
+thff_status thff_conv1d_async(int dtype, int n, int lin, const void* d_x, const void* d_spectrum, void* d_y,
+                              long long batch, void* stream) {
+  if (dtype != THFF_F32) return fail(THFF_INVALID_ARGUMENT, "conv1d: float storage only");
+  if (n != 1024 && n != 4096) return fail(THFF_INVALID_ARGUMENT, "conv1d: n must be 1024 or 4096");
+  const int L = n == 4096 ? 64 : 32;
+  if (lin <= 0 || lin > n || lin % L != 0)
+    return fail(THFF_INVALID_ARGUMENT, "conv1d: input length must be a positive multiple of sqrt(n), <= n");
+  if (batch < 0) return fail(THFF_INVALID_ARGUMENT, "conv1d: batch must be nonnegative");
+  if (batch == 0) return THFF_OK;
+  if (!d_x || !d_spectrum || !d_y) return fail(THFF_INVALID_ARGUMENT, "conv1d: null pointer");
+  if (!aligned16(d_x) || !aligned16(d_spectrum) || (reinterpret_cast<uintptr_t>(d_y) & 7u))
+    return fail(THFF_INVALID_ARGUMENT, "conv1d: x and spectrum must be 16-byte aligned, y 8-byte aligned");
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  DeviceState* st;
+  const Consts* c;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
+    if ((s = get_conv_consts(*st, n, &c)) != THFF_OK) return s;
+  }
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  return n == 4096 ? launch_conv1d<4096>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs)
+                   : launch_conv1d<1024>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs);
+}
+
+thff_status thff_conv1d(int dtype, int n, int lin, const void* d_x, const void* d_spectrum, void* d_y,
+                        long long batch, void* stream) {
+  thff_status s = thff_conv1d_async(dtype, n, lin, d_x, d_spectrum, d_y, batch, stream);
+  if (s != THFF_OK || batch == 0) return s;
   return thff_sync_check(stream);
 }
 
