@@ -75,6 +75,13 @@ thff_status thff_c2c_async(int dtype, int n, int forward, const void* d_input, v
 thff_status thff_sync_check(void* stream);
 
 
+/* Failure-detection self-test (no reference counterpart): launches a kernel
+ * whose bounded mbarrier wait can never be satisfied and must give up after
+ * limit_us microseconds.  Returns THFF_DEVICE_TIMEOUT when the device-side
+ * timeout path works (the CUDA context stays usable), THFF_OK if it did not
+ * trigger, or a CUDA error. */
+thff_status thff_selftest_wait_timeout(int limit_us, void* stream);
+
 /* ---- fused real 1-D FFT convolution --------------------------------------
  * Counterpart of the reference's fused conv1d sample
  * (sample/conv1d/conv1d_fullfft_l4096_thunder.cu:280-331), here for float

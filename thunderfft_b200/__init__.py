@@ -79,6 +79,8 @@ def load_library() -> ctypes.CDLL:
     lib.thff_conv1d_filter_spectrum.argtypes = [i32, i32, vp, i32, vp, vp]
     lib.thff_conv1d_async.argtypes = [i32, i32, i32, vp, vp, vp, i64, vp]
     lib.thff_conv1d.argtypes = [i32, i32, i32, vp, vp, vp, i64, vp]
+    lib.thff_selftest_wait_timeout.argtypes = [i32, vp]
+    lib.thff_selftest_wait_timeout.restype = i32
     for name in ("thff_initialize", "thff_finalize", "thff_twiddle_table", "thff_global",
                  "thff_c2c_async", "thff_sync_check", "thff_conv1d_filter_spectrum", "thff_conv1d_async",
                  "thff_conv1d"):

@@ -639,4 +639,16 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
   }
 }
 
+// Failure-detection self-test: one thread waits on an mbarrier that nothing
+// will ever arrive on; the bounded wait must give up after `limit_ns`,
+// record kDevTimeoutOther in *err and let the kernel exit normally.
+__global__ void wait_timeout_selftest_kernel(uint32_t* err, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    sm100::fence_mbar_init();
+    sm100::mbar_wait_limit(&bar, 0, err, sm100::kDevTimeoutOther, limit_ns);
+  }
+}
+
 }  // namespace thff

@@ -95,6 +95,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   }
 }
 
+// Same wait with a caller-chosen wall-clock limit (used by the self-test that
+// proves a stalled wait ends with an error status instead of a hang).
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                                uint32_t code, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      atomicCAS(err, 0u, code);
+      return false;
+    }
+  }
+}
+
 // Warp-uniform variant: every lane waits (so each lane acquires the phase),
 // and the warp agrees on the outcome so that no lane leaves a loop while the
 // others go on to warp-collective instructions.

@@ -126,11 +126,6 @@ std::vector<uint8_t> build_dft1_matrix(int N, int sign, bool half) {
 // ---------------------------------------------------------------------------
 // Per-device state
 // ---------------------------------------------------------------------------
-struct DevBuf {
-  void* p = nullptr;
-  ~DevBuf() {}
-};
-
 struct Consts {            // per (dtype, N, direction)
   void* a1 = nullptr;      // stage-1 A image (or the one-stage DFT matrix)
   void* a2 = nullptr;      // stage-2 A image
@@ -547,6 +542,22 @@ thff_status thff_global(int dtype, int n, int forward, const void* d_input, void
   thff_status s = thff_c2c_async(dtype, n, forward, d_input, d_output, batch, stream);
   if (s != THFF_OK) return s;
   return thff_sync_check(stream);
+}
+
+thff_status thff_selftest_wait_timeout(int limit_us, void* stream) {
+  if (limit_us <= 0 || limit_us > 1000000) return fail(THFF_INVALID_ARGUMENT, "selftest: limit must be in (0, 1e6] us");
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  DeviceState* st;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
+  }
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  thff::wait_timeout_selftest_kernel<<<1, 32, 0, cs>>>(st->d_err, 1000ull * (unsigned long long)limit_us);
+  THFF_CUDA(cudaGetLastError(), "selftest launch");
+  return read_device_error(*st, cs);
 }
 
 long long thff_conv1d_spectrum_bytes(int dtype, int n) {
