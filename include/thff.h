@@ -109,6 +109,36 @@ thff_status thff_conv1d_async(int dtype, int n, int lin, const void* d_x, const 
 thff_status thff_conv1d(int dtype, int n, int lin, const void* d_x, const void* d_spectrum, void* d_y,
                         long long batch, void* stream);
 
+/* ---- 2-D FFT convolution --------------------------------------------------
+ * Counterpart of the reference's 2-D FFT convolution sample
+ * (sample/conv2d/thunder.cu:70-207,410-592: row FFT, column FFT x H x
+ * column IFFT, row IFFT), here for real fp32 images x[B][C][h][w] with one
+ * real f x f filter per channel and circular convolution:
+ *     y[b][c][i][j] = sum_{u,v<f} filt[c][u][v] * x[b][c][(i-u) mod h][(j-v) mod w].
+ * Images b and b+1 of a channel share one complex 2-D transform.  h, w in
+ * {128, ..., 4096}.  The caller provides scratch: a workspace of
+ * thff_conv2d_workspace_bytes(..., pairs) bytes processes `pairs` image
+ * pairs per pass (any size >= one pair works; larger is faster). */
+
+/* Workspace bytes for processing `pairs` image pairs at a time. */
+long long thff_conv2d_workspace_bytes(int dtype, int h, int w, long long pairs);
+
+/* spectra[c][k2][k1] = (1/(h*w)) * sum_{u,v} filt[c][u][v] exp(-2 pi i (u k1/h + v k2/w)),
+ * complex fp32 (c*h*w entries); needs channels*f*w*16 bytes of workspace. */
+thff_status thff_conv2d_filter_spectra(int dtype, int h, int w, int channels, int f, const float* d_filters,
+                                       void* d_spectra, void* d_workspace, long long workspace_bytes,
+                                       void* stream);
+
+/* Asynchronous 2-D convolution of all B*C images (see above). */
+thff_status thff_conv2d_async(int dtype, long long batch, int channels, int h, int w, const void* d_x,
+                              const void* d_spectra, void* d_y, void* d_workspace, long long workspace_bytes,
+                              void* stream);
+
+/* Same, then synchronizes `stream` and reports device-side errors. */
+thff_status thff_conv2d(int dtype, long long batch, int channels, int h, int w, const void* d_x,
+                        const void* d_spectra, void* d_y, void* d_workspace, long long workspace_bytes,
+                        void* stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

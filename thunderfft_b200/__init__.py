@@ -34,6 +34,7 @@ __all__ = [
     "ThunderFFTInitialize", "ThunderFFTFinalize", "ThunderFFT_global", "c2c_async", "sync_check",
     "twiddle_table", "fft", "load_library", "library_path", "SUPPORTED_N", "batch_per_block",
     "warp_per_block", "threads_per_warp", "version", "conv1d_filter_spectrum", "conv1d",
+    "conv2d_filter_spectra", "conv2d", "conv2d_workspace",
 ]
 
 SUPPORTED_N = (64, 128, 256, 512, 1024, 2048, 4096)
@@ -79,6 +80,14 @@ def load_library() -> ctypes.CDLL:
     lib.thff_conv1d_filter_spectrum.argtypes = [i32, i32, vp, i32, vp, vp]
     lib.thff_conv1d_async.argtypes = [i32, i32, i32, vp, vp, vp, i64, vp]
     lib.thff_conv1d.argtypes = [i32, i32, i32, vp, vp, vp, i64, vp]
+    lib.thff_conv2d_workspace_bytes.argtypes = [i32, i32, i32, i64]
+    lib.thff_conv2d_workspace_bytes.restype = i64
+    lib.thff_conv2d_filter_spectra.argtypes = [i32, i32, i32, i32, i32, vp, vp, vp, i64, vp]
+    lib.thff_conv2d_filter_spectra.restype = i32
+    lib.thff_conv2d_async.argtypes = [i32, i64, i32, i32, i32, vp, vp, vp, vp, i64, vp]
+    lib.thff_conv2d_async.restype = i32
+    lib.thff_conv2d.argtypes = [i32, i64, i32, i32, i32, vp, vp, vp, vp, i64, vp]
+    lib.thff_conv2d.restype = i32
     lib.thff_selftest_wait_timeout.argtypes = [i32, vp]
     lib.thff_selftest_wait_timeout.restype = i32
     for name in ("thff_initialize", "thff_finalize", "thff_twiddle_table", "thff_global",
@@ -232,4 +241,50 @@ def conv1d(x, spectrum, n: int, out=None, stream=None, sync: bool = True):
     fn = load_library().thff_conv1d if sync else load_library().thff_conv1d_async
     _check(fn(0, int(n), int(lin), x.data_ptr(), spectrum.data_ptr(), out.data_ptr(), int(batch),
               _stream_handle(st)))
+    return out
+
+
+def conv2d_workspace(h: int, w: int, pairs: int, device=None):
+    """Allocate a conv2d workspace (uint8 CUDA tensor) for `pairs` image pairs per pass."""
+    import torch
+
+    n = load_library().thff_conv2d_workspace_bytes(0, int(h), int(w), int(pairs))
+    if n <= 0:
+        raise ValueError("unsupported conv2d shape")
+    return torch.empty(n, dtype=torch.uint8, device=device or "cuda")
+
+
+def conv2d_filter_spectra(filters, h: int, w: int, stream=None):
+    """Spectra of real per-channel filters (float32 CUDA tensor [C, f, f]) for
+    `conv2d`: complex64 [C, w, h] (transposed), 1/(h w) folded in."""
+    import torch
+
+    if not (filters.is_cuda and filters.dtype == torch.float32 and filters.dim() == 3 and filters.is_contiguous()):
+        raise ValueError("filters must be a contiguous [C, f, f] float32 CUDA tensor")
+    C, f, f2 = filters.shape
+    if f != f2:
+        raise ValueError("filters must be square")
+    spec = torch.empty(C, w, h, dtype=torch.complex64, device=filters.device)
+    ws = torch.empty(C * f * w * 16, dtype=torch.uint8, device=filters.device)
+    st = stream if stream is not None else torch.cuda.current_stream(filters.device)
+    _check(load_library().thff_conv2d_filter_spectra(0, int(h), int(w), int(C), int(f), filters.data_ptr(),
+                                                      spec.data_ptr(), ws.data_ptr(), ws.numel(), _stream_handle(st)))
+    return spec
+
+
+def conv2d(x, spectra, workspace, out=None, stream=None, sync: bool = True):
+    """Circular 2-D convolution of real images x (float32 CUDA [B, C, h, w])
+    with per-channel filters given by `conv2d_filter_spectra`.  `workspace`
+    is caller-owned scratch from `conv2d_workspace`."""
+    import torch
+
+    if not (x.is_cuda and x.dtype == torch.float32 and x.dim() == 4 and x.is_contiguous()):
+        raise ValueError("x must be a contiguous [B, C, h, w] float32 CUDA tensor")
+    B, C, h, w = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    fn = load_library().thff_conv2d if sync else load_library().thff_conv2d_async
+    _check(fn(0, int(B), int(C), int(h), int(w), x.data_ptr(), spectra.data_ptr(), out.data_ptr(),
+              workspace.data_ptr(), workspace.numel(), _stream_handle(st)))
     return out

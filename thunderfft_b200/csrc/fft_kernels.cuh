@@ -136,6 +136,22 @@ struct FftParams {
   long long batch;
   int use_tma;           // input tiles via TMA (aligned input) or thread loads
   uint32_t* err;         // device error word (0 = ok)
+  // Output modes of the stage-2 epilogue used by the 2-D convolution
+  // (kEpi != 0 only; the C2C API uses the natural layout):
+  const float2* spec;    // kEpiMul: out *= spec[((sig/R + pair0) % C)*R + sig%R][k]
+  long long rows;        // R: signals per image
+  long long pair0;       // first image pair of this launch
+  int chans;             // C
+  long long nimg_b;      // B (images per channel) for the pair-unpack store
+};
+
+// Stage-2 epilogue output modes.
+enum EpiMode : int {
+  kEpiNatural = 0,        // out[sig][k]
+  kEpiTransposeMul = 1,   // out[img][k][r] (sig = img*R + r), optionally * spectrum
+  kEpiTranspose = 2,      // out[img][k][r]
+  kEpiMulNatural = 3,     // out[sig][k] * spectrum
+  kEpiUnpackPair = 4,     // real fp32 images: Re -> x[b][ch][r][k], Im -> x[b+1][ch][r][k]
 };
 
 namespace detail {
@@ -179,7 +195,7 @@ __device__ __forceinline__ uint32_t in_tile_offset(int sig, int s, int a) {
 // ---------------------------------------------------------------------------
 // Two-stage kernel
 // ---------------------------------------------------------------------------
-template <class C>
+template <class C, int kEpi = kEpiNatural>
 __global__ void __launch_bounds__(C::kThreads, 1)
 fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
   using namespace sm100;
@@ -409,8 +425,33 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
             const float rr = __uint_as_float(r[4 * j + 0]), ri = __uint_as_float(r[4 * j + 1]);
             const float ir = __uint_as_float(r[4 * j + 2]), ii = __uint_as_float(r[4 * j + 3]);
             const long long sig = sig0 + g2 * C::C2 + c2;
-            if (sig < batch)
-              detail::store_out<C::kIsHalf>(p.out, sig * C::N + (long long)C::NS * ka + ks, rr - ii, ir + ri);
+            if (sig < batch) {
+              const long long k = (long long)C::NS * ka + ks;
+              float xr = rr - ii, xi = ir + ri;
+              if constexpr (kEpi == kEpiNatural) {
+                detail::store_out<C::kIsHalf>(p.out, sig * C::N + k, xr, xi);
+              } else {
+                const long long img = sig / p.rows, r = sig % p.rows;
+                if constexpr (kEpi == kEpiTransposeMul || kEpi == kEpiMulNatural) {
+                  const float2 w = __ldg(p.spec + (((img + p.pair0) % p.chans) * p.rows + r) * C::N + k);
+                  const float tr = xr * w.x - xi * w.y;
+                  xi = xr * w.y + xi * w.x;
+                  xr = tr;
+                }
+                if constexpr (kEpi == kEpiTransposeMul || kEpi == kEpiTranspose) {
+                  detail::store_out<C::kIsHalf>(p.out, (img * C::N + k) * p.rows + r, xr, xi);
+                } else if constexpr (kEpi == kEpiMulNatural) {
+                  detail::store_out<C::kIsHalf>(p.out, sig * C::N + k, xr, xi);
+                } else {
+                  // pair p -> images (b, ch), (b+1, ch); fp32 real output
+                  const long long pr = img + p.pair0, b = 2 * (pr / p.chans), ch = pr % p.chans;
+                  float* y = reinterpret_cast<float*>(p.out);
+                  const long long o = ((b * p.chans + ch) * p.rows + r) * C::N + k;
+                  y[o] = xr;
+                  if (b + 1 < p.nimg_b) y[o + (long long)p.chans * p.rows * C::N] = xi;
+                }
+              }
+            }
           }
         }
       }

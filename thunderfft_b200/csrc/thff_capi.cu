@@ -22,6 +22,7 @@
 #include "../../include/thff.h"
 #include "fft_kernels.cuh"
 #include "conv1d_kernel.cuh"
+#include "conv2d_kernels.cuh"
 
 namespace {
 
@@ -266,9 +267,9 @@ thff_status set_smem_attr(DeviceState& st, K kernel, int bytes) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <bool kHalf, int kN>
+template <bool kHalf, int kN, int kEpi = thff::kEpiNatural>
 thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* out, long long batch,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const thff::FftParams* extra = nullptr) {
   using C = thff::Fft2Cfg<kHalf, kN>;
   const long long num_tiles = (batch + C::T - 1) / C::T;
   const long long full_tiles = batch / C::T;
@@ -295,7 +296,9 @@ thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* 
   thff::FftParams p;
   p.in = in; p.out = out; p.a1 = c.a1; p.a2 = c.a2; p.tw = reinterpret_cast<const float2*>(c.tw);
   p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = st.d_err;
-  auto kernel = thff::fft2_kernel<C>;
+  p.spec = nullptr; p.rows = 1; p.pair0 = 0; p.chans = 1; p.nimg_b = 0;
+  if (extra) { p.spec = extra->spec; p.rows = extra->rows; p.pair0 = extra->pair0; p.chans = extra->chans; p.nimg_b = extra->nimg_b; }
+  auto kernel = thff::fft2_kernel<C, kEpi>;
   thff_status s = set_smem_attr(st, kernel, int(C::SMEM_BYTES));
   if (s != THFF_OK) return s;
   const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
@@ -400,6 +403,30 @@ thff_status get_conv_consts(DeviceState& st, int n, const Consts** out) {
   *out = &it->second;
   return THFF_OK;
 }
+
+// One pass of the 2-D convolution pipeline: length-n C2C transform of
+// `batch` signals with the stage-2 epilogue in mode kEpi.
+template <int kEpi>
+thff_status conv2d_pass(DeviceState& st, int n, bool fwd, const void* in, void* out, long long batch,
+                        const thff::FftParams& extra, cudaStream_t cs) {
+  const Consts* c;
+  thff_status s;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if ((s = get_consts(st, THFF_F32, n, fwd, &c)) != THFF_OK) return s;
+  }
+  switch (n) {
+    case 128: return launch_fft2<false, 128, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 256: return launch_fft2<false, 256, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 512: return launch_fft2<false, 512, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 1024: return launch_fft2<false, 1024, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 2048: return launch_fft2<false, 2048, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 4096: return launch_fft2<false, 4096, kEpi>(st, *c, in, out, batch, cs, &extra);
+  }
+  return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
+}
+
+bool conv2d_side_ok(int v) { return v == 128 || v == 256 || v == 512 || v == 1024 || v == 2048 || v == 4096; }
 
 thff_status read_device_error(DeviceState& st, cudaStream_t stream) {
   if (!t_err_host) THFF_CUDA(cudaMallocHost(&t_err_host, sizeof(uint32_t)), "cudaMallocHost(error word)");
@@ -608,6 +635,88 @@ thff_status thff_conv1d(int dtype, int n, int lin, const void* d_x, const void* 
                         long long batch, void* stream) {
   thff_status s = thff_conv1d_async(dtype, n, lin, d_x, d_spectrum, d_y, batch, stream);
   if (s != THFF_OK || batch == 0) return s;
+  return thff_sync_check(stream);
+}
+
+long long thff_conv2d_workspace_bytes(int dtype, int h, int w, long long pairs) {
+  if (dtype != THFF_F32 || !conv2d_side_ok(h) || !conv2d_side_ok(w) || pairs <= 0) return -1;
+  return 2LL * pairs * h * w * 8;
+}
+
+thff_status thff_conv2d_filter_spectra(int dtype, int h, int w, int chans, int f, const float* d_filters,
+                                       void* d_spectra, void* d_workspace, long long workspace_bytes,
+                                       void* stream) {
+  if (dtype != THFF_F32) return fail(THFF_INVALID_ARGUMENT, "conv2d: float storage only");
+  if (!conv2d_side_ok(h) || !conv2d_side_ok(w)) return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
+  if (chans <= 0 || f <= 0 || f > h || f > w) return fail(THFF_INVALID_ARGUMENT, "conv2d: need channels > 0 and 0 < filter size <= image side");
+  if (!d_filters || !d_spectra || !d_workspace) return fail(THFF_INVALID_ARGUMENT, "conv2d: null pointer");
+  const long long need = (long long)chans * f * w * 16;
+  if (workspace_bytes < need) return fail(THFF_INVALID_ARGUMENT, "conv2d: filter workspace too small (need channels*f*w*16 bytes)");
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  double2* g = static_cast<double2*>(d_workspace);
+  const long long n1 = (long long)chans * f * w, n2 = (long long)chans * h * w;
+  thff::conv2d_filter_rows_kernel<<<unsigned((n1 + 255) / 256), 256, 0, cs>>>(d_filters, chans, f, w, g);
+  THFF_CUDA(cudaGetLastError(), "conv2d filter spectrum launch");
+  thff::conv2d_filter_cols_kernel<<<unsigned((n2 + 255) / 256), 256, 0, cs>>>(g, chans, f, h, w, static_cast<float2*>(d_spectra));
+  THFF_CUDA(cudaGetLastError(), "conv2d filter spectrum launch");
+  return THFF_OK;
+}
+
+thff_status thff_conv2d_async(int dtype, long long nimg_b, int chans, int h, int w, const void* d_x,
+                              const void* d_spectra, void* d_y, void* d_workspace, long long workspace_bytes,
+                              void* stream) {
+  if (dtype != THFF_F32) return fail(THFF_INVALID_ARGUMENT, "conv2d: float storage only");
+  if (!conv2d_side_ok(h) || !conv2d_side_ok(w)) return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
+  if (nimg_b < 0 || chans <= 0) return fail(THFF_INVALID_ARGUMENT, "conv2d: need batch >= 0 and channels > 0");
+  if (nimg_b == 0) return THFF_OK;
+  if (!d_x || !d_spectra || !d_y || !d_workspace) return fail(THFF_INVALID_ARGUMENT, "conv2d: null pointer");
+  if (!aligned16(d_x) || !aligned16(d_y) || !aligned16(d_workspace) || !aligned16(d_spectra))
+    return fail(THFF_INVALID_ARGUMENT, "conv2d: buffers must be 16-byte aligned");
+  const long long per_pair = 2LL * h * w * 8;
+  const long long chunk = workspace_bytes / per_pair;
+  if (chunk < 1) return fail(THFF_INVALID_ARGUMENT, "conv2d: workspace smaller than one image pair (2*h*w*16 bytes)");
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  DeviceState* st;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
+  }
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const long long pairs = ((nimg_b + 1) / 2) * chans;
+  float2* z0 = static_cast<float2*>(d_workspace);
+  float2* z1 = z0 + (size_t)chunk * h * w;
+  const long long hw = (long long)h * w;
+  for (long long p0 = 0; p0 < pairs; p0 += chunk) {
+    const long long np = (pairs - p0 < chunk) ? pairs - p0 : chunk;
+    const long long n4 = np * hw / 4;
+    thff::conv2d_pack_kernel<<<unsigned((n4 + 255) / 256), 256, 0, cs>>>(
+        static_cast<const float*>(d_x), z0, int(nimg_b), chans, int(hw), p0, np);
+    THFF_CUDA(cudaGetLastError(), "conv2d pack launch");
+    thff::FftParams ex;
+    std::memset(&ex, 0, sizeof(ex));
+    ex.chans = chans; ex.pair0 = p0; ex.nimg_b = nimg_b; ex.spec = static_cast<const float2*>(d_spectra);
+    // rows forward, written transposed: z1[p][k2][r]
+    ex.rows = h;
+    if ((s = conv2d_pass<thff::kEpiTranspose>(*st, w, true, z0, z1, np * h, ex, cs)) != THFF_OK) return s;
+    // columns forward, times the spectrum: z0[p][k2][k1]
+    ex.rows = w;
+    if ((s = conv2d_pass<thff::kEpiMulNatural>(*st, h, true, z1, z0, np * w, ex, cs)) != THFF_OK) return s;
+    // columns inverse, written transposed back: z1[p][r][k2]
+    if ((s = conv2d_pass<thff::kEpiTranspose>(*st, h, false, z0, z1, np * w, ex, cs)) != THFF_OK) return s;
+    // rows inverse, real/imaginary parts to the two images of each pair
+    ex.rows = h;
+    if ((s = conv2d_pass<thff::kEpiUnpackPair>(*st, w, false, z1, d_y, np * h, ex, cs)) != THFF_OK) return s;
+  }
+  return THFF_OK;
+}
+
+thff_status thff_conv2d(int dtype, long long nimg_b, int chans, int h, int w, const void* d_x, const void* d_spectra,
+                        void* d_y, void* d_workspace, long long workspace_bytes, void* stream) {
+  thff_status s = thff_conv2d_async(dtype, nimg_b, chans, h, w, d_x, d_spectra, d_y, d_workspace, workspace_bytes,
+                                    stream);
+  if (s != THFF_OK || nimg_b == 0) return s;
   return thff_sync_check(stream);
 }
 
