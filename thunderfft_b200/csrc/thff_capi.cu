@@ -428,6 +428,50 @@ thff_status conv2d_pass(DeviceState& st, int n, bool fwd, const void* in, void* 
 
 bool conv2d_side_ok(int v) { return v == 128 || v == 256 || v == 512 || v == 1024 || v == 2048 || v == 4096; }
 
+// ---------------------------------------------------------------------------
+// Allocation-free 2-D convolution (thff_conv2d_noalloc)
+//
+// Some callers cannot call cudaMalloc at the point where they run the
+// convolution: code recorded into a CUDA graph by stream capture (cudaMalloc
+// would break the capture), plugins and real-time pipelines whose host
+// application owns all device memory and forbids allocation on the hot path,
+// and frameworks whose pooling allocator must account for every byte.  For
+// them the scratch of the 2-D convolution lives in this fixed device array
+// instead of a caller workspace.  Every GPU that loads the library holds it
+// (kNoAllocScratchBytes) until the process exits.
+// ---------------------------------------------------------------------------
+constexpr long long kNoAllocScratchBytes = 16LL << 20;  // 16 MiB: one pass holds scratch/(2*h*w*16) image pairs
+static __device__ __align__(256) unsigned char g_conv2d_scratch[kNoAllocScratchBytes];
+std::map<int, void*> g_noalloc_scratch;  // device -> address of g_conv2d_scratch (under g_mutex)
+
+// Look up FFT constants without building them (building would allocate).
+const Consts* find_consts(DeviceState& st, int dtype, int n, bool fwd) {
+  auto it = st.consts.find((dtype * 2 + (fwd ? 1 : 0)) * 8192 + n);
+  return it == st.consts.end() ? nullptr : &it->second;
+}
+
+template <int kEpi>
+thff_status conv2d_pass_noalloc(DeviceState& st, int n, bool fwd, const void* in, void* out, long long batch,
+                                const thff::FftParams& extra, cudaStream_t cs) {
+  const Consts* c;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    c = find_consts(st, THFF_F32, n, fwd);
+  }
+  if (!c)
+    return fail(THFF_INVALID_ARGUMENT, "thff_conv2d_noalloc: call thff_initialize(THFF_F32, " + std::to_string(n) +
+                                           ") on this device first (this entry point allocates nothing)");
+  switch (n) {
+    case 128: return launch_fft2<false, 128, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 256: return launch_fft2<false, 256, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 512: return launch_fft2<false, 512, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 1024: return launch_fft2<false, 1024, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 2048: return launch_fft2<false, 2048, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 4096: return launch_fft2<false, 4096, kEpi>(st, *c, in, out, batch, cs, &extra);
+  }
+  return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
+}
+
 thff_status read_device_error(DeviceState& st, cudaStream_t stream) {
   if (!t_err_host) THFF_CUDA(cudaMallocHost(&t_err_host, sizeof(uint32_t)), "cudaMallocHost(error word)");
   *t_err_host = 0;
@@ -718,6 +762,69 @@ thff_status thff_conv2d(int dtype, long long nimg_b, int chans, int h, int w, co
                                     stream);
   if (s != THFF_OK || nimg_b == 0) return s;
   return thff_sync_check(stream);
+}
+
+thff_status thff_conv2d_noalloc(int dtype, long long nimg_b, int chans, int h, int w, const void* d_x,
+                                const void* d_spectra, void* d_y, void* stream) {
+  if (dtype != THFF_F32) return fail(THFF_INVALID_ARGUMENT, "conv2d: float storage only");
+  if (!conv2d_side_ok(h) || !conv2d_side_ok(w)) return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
+  if (nimg_b < 0 || chans <= 0) return fail(THFF_INVALID_ARGUMENT, "conv2d: need batch >= 0 and channels > 0");
+  const long long per_pair = 2LL * h * w * 8;
+  if (per_pair > kNoAllocScratchBytes)
+    return fail(THFF_INVALID_ARGUMENT, "thff_conv2d_noalloc: an image pair needs " + std::to_string(per_pair) +
+                                           " bytes of scratch but the fixed scratch holds " +
+                                           std::to_string(kNoAllocScratchBytes) + " (h*w must be <= 1048576)");
+  if (nimg_b == 0) return THFF_OK;
+  if (!d_x || !d_spectra || !d_y) return fail(THFF_INVALID_ARGUMENT, "conv2d: null pointer");
+  if (!aligned16(d_x) || !aligned16(d_y) || !aligned16(d_spectra))
+    return fail(THFF_INVALID_ARGUMENT, "conv2d: buffers must be 16-byte aligned");
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  DeviceState* st = nullptr;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_dev.find(dev);
+    if (it == g_dev.end() || !it->second.ready)
+      return fail(THFF_INVALID_ARGUMENT, "thff_conv2d_noalloc: call thff_initialize on this device first "
+                                         "(this entry point allocates nothing)");
+    st = &it->second;
+    auto sc = g_noalloc_scratch.find(dev);
+    if (sc == g_noalloc_scratch.end()) {
+      // first call on this device: resolve the device address of the array
+      void* ptr = nullptr;
+      THFF_CUDA(cudaGetSymbolAddress(&ptr, g_conv2d_scratch), "cudaGetSymbolAddress(conv2d scratch)");
+      sc = g_noalloc_scratch.emplace(dev, ptr).first;
+    }
+    scratch = sc->second;
+  }
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const long long chunk = kNoAllocScratchBytes / per_pair;
+  const long long pairs = ((nimg_b + 1) / 2) * chans;
+  float2* z0 = static_cast<float2*>(scratch);
+  float2* z1 = z0 + (size_t)chunk * h * w;
+  const long long hw = (long long)h * w;
+  // Every pass below writes its whole output region before the next pass
+  // reads it, so nothing left in the scratch by an earlier call is read.
+  for (long long p0 = 0; p0 < pairs; p0 += chunk) {
+    const long long np = (pairs - p0 < chunk) ? pairs - p0 : chunk;
+    const long long n4 = np * hw / 4;
+    thff::conv2d_pack_kernel<<<unsigned((n4 + 255) / 256), 256, 0, cs>>>(
+        static_cast<const float*>(d_x), z0, int(nimg_b), chans, int(hw), p0, np);
+    THFF_CUDA(cudaGetLastError(), "conv2d pack launch");
+    thff::FftParams ex;
+    std::memset(&ex, 0, sizeof(ex));
+    ex.chans = chans; ex.pair0 = p0; ex.nimg_b = nimg_b; ex.spec = static_cast<const float2*>(d_spectra);
+    ex.rows = h;
+    if ((s = conv2d_pass_noalloc<thff::kEpiTranspose>(*st, w, true, z0, z1, np * h, ex, cs)) != THFF_OK) return s;
+    ex.rows = w;
+    if ((s = conv2d_pass_noalloc<thff::kEpiMulNatural>(*st, h, true, z1, z0, np * w, ex, cs)) != THFF_OK) return s;
+    if ((s = conv2d_pass_noalloc<thff::kEpiTranspose>(*st, h, false, z0, z1, np * w, ex, cs)) != THFF_OK) return s;
+    ex.rows = h;
+    if ((s = conv2d_pass_noalloc<thff::kEpiUnpackPair>(*st, w, false, z1, d_y, np * h, ex, cs)) != THFF_OK) return s;
+  }
+  return THFF_OK;
 }
 
 }  // extern "C"
