@@ -47,7 +47,7 @@ struct Conv1dCfg {
   static constexpr uint32_t OFF_A = 0;
   static constexpr uint32_t OFF_IN = (A_BYTES + 1023) / 1024 * 1024;
   static constexpr uint32_t OFF_B = OFF_IN + SIN * TILE_BYTES;   // B2, B3, B4
-  static constexpr uint32_t SMEM_BYTES = OFF_B + 3 * TILE_BYTES + 1024;
+  static constexpr uint32_t SMEM_BYTES = exclusive_smem(OFF_B + 3 * TILE_BYTES + 1024);
   static_assert(SMEM_BYTES + 1024 <= 232448, "shared memory budget");
   static_assert(M == 128 ? NCOL <= 128 : NCOL <= 256, "TMEM budget (4 accumulators)");
   static constexpr int kThreads = 320;

@@ -41,6 +41,16 @@
 
 namespace thff {
 
+// Every kernel here is persistent (one CTA per SM) and allocates all 512 TMEM
+// columns.  A second CTA resident on the same SM would block in tcgen05.alloc
+// until the first exits, leaving other SMs idle, so each launch requests at
+// least this much dynamic shared memory: more than half of an SM's 228 KB
+// makes a second resident CTA impossible regardless of register use.
+constexpr uint32_t kExclusiveSmemBytes = 120u * 1024u;
+__host__ __device__ constexpr uint32_t exclusive_smem(uint32_t bytes) {
+  return bytes > kExclusiveSmemBytes ? bytes : kExclusiveSmemBytes;
+}
+
 // ---------------------------------------------------------------------------
 // Storage/arithmetic traits: float2 storage -> kind::tf32; half2 -> kind::f16.
 // ---------------------------------------------------------------------------
@@ -76,19 +86,19 @@ struct DType<true> {
 template <bool kHalf, int kN>
 struct Fft2Shape;
 // float2 / tf32
-template <> struct Fft2Shape<false, 128>  { static constexpr int NS = 8,  NA = 16, G1 = 4, G2 = 2, T = 32, SIN = 4; };
-template <> struct Fft2Shape<false, 256>  { static constexpr int NS = 16, NA = 16, G1 = 2, G2 = 2, T = 16, SIN = 4; };
-template <> struct Fft2Shape<false, 512>  { static constexpr int NS = 32, NA = 16, G1 = 1, G2 = 2, T = 8,  SIN = 4; };
-template <> struct Fft2Shape<false, 1024> { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 4; };
-template <> struct Fft2Shape<false, 2048> { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 3; };
-template <> struct Fft2Shape<false, 4096> { static constexpr int NS = 64, NA = 64, G1 = 1, G2 = 1, T = 1,  SIN = 2; };
+template <> struct Fft2Shape<false, 128>  { static constexpr int NS = 8,  NA = 16, G1 = 4, G2 = 2, T = 32, SIN = 4, EPW = 1; };
+template <> struct Fft2Shape<false, 256>  { static constexpr int NS = 16, NA = 16, G1 = 2, G2 = 2, T = 16, SIN = 4, EPW = 1; };
+template <> struct Fft2Shape<false, 512>  { static constexpr int NS = 32, NA = 16, G1 = 1, G2 = 2, T = 8,  SIN = 4, EPW = 2; };
+template <> struct Fft2Shape<false, 1024> { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 4, EPW = 2; };
+template <> struct Fft2Shape<false, 2048> { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 3, EPW = 2; };
+template <> struct Fft2Shape<false, 4096> { static constexpr int NS = 64, NA = 64, G1 = 1, G2 = 1, T = 1,  SIN = 2, EPW = 1; };
 // half2 / f16
-template <> struct Fft2Shape<true, 128>   { static constexpr int NS = 4,  NA = 32, G1 = 8, G2 = 1, T = 32, SIN = 4; };
-template <> struct Fft2Shape<true, 256>   { static constexpr int NS = 8,  NA = 32, G1 = 4, G2 = 1, T = 16, SIN = 4; };
-template <> struct Fft2Shape<true, 512>   { static constexpr int NS = 16, NA = 32, G1 = 2, G2 = 1, T = 8,  SIN = 4; };
-template <> struct Fft2Shape<true, 1024>  { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 4; };
-template <> struct Fft2Shape<true, 2048>  { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 4; };
-template <> struct Fft2Shape<true, 4096>  { static constexpr int NS = 64, NA = 64, G1 = 1, G2 = 1, T = 1,  SIN = 4; };
+template <> struct Fft2Shape<true, 128>   { static constexpr int NS = 4,  NA = 32, G1 = 8, G2 = 1, T = 32, SIN = 8, EPW = 1; };
+template <> struct Fft2Shape<true, 256>   { static constexpr int NS = 8,  NA = 32, G1 = 4, G2 = 1, T = 16, SIN = 8, EPW = 1; };
+template <> struct Fft2Shape<true, 512>   { static constexpr int NS = 16, NA = 32, G1 = 2, G2 = 1, T = 8,  SIN = 8, EPW = 1; };
+template <> struct Fft2Shape<true, 1024>  { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 8, EPW = 1; };
+template <> struct Fft2Shape<true, 2048>  { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 8, EPW = 1; };
+template <> struct Fft2Shape<true, 4096>  { static constexpr int NS = 64, NA = 64, G1 = 1, G2 = 1, T = 1,  SIN = 8, EPW = 1; };
 
 template <bool kHalf, int kN>
 struct Fft2Cfg {
@@ -121,9 +131,11 @@ struct Fft2Cfg {
   static constexpr uint32_t OFF_IN = OFF_A2 + (A2_BYTES + 1023) / 1024 * 1024;
   static constexpr uint32_t OFF_Y = OFF_IN + SIN * TILE_BYTES;
   static constexpr uint32_t SMEM_DATA = OFF_Y + 2 * TILE_BYTES;
-  static constexpr uint32_t SMEM_BYTES = SMEM_DATA + 1024 /*align slack*/;
+  static constexpr uint32_t SMEM_BYTES = exclusive_smem(SMEM_DATA + 1024 /*align slack*/);
   static_assert(SMEM_BYTES + 512 <= 232448, "shared memory budget");
-  static constexpr int kThreads = 320;                     // 10 warps
+  static constexpr int EPW = S::EPW;                       // epilogue warps per TMEM lane quadrant
+  static constexpr int kEpiWarps = 4 * EPW;                // per epilogue stage
+  static constexpr int kThreads = 32 * (2 + 2 * kEpiWarps); // producer, MMA, 2 x 8 epilogue warps
 };
 
 // Host-visible kernel parameters (besides tensor maps).
@@ -217,9 +229,9 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::SIN; ++i) { mbar_init(&bar_in_full[i], 1); mbar_init(&bar_in_empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bar_acc1_full[i], 1); mbar_init(&bar_acc1_empty[i], 4);
-      mbar_init(&bar_y_full[i], 4);    mbar_init(&bar_y_empty[i], 1);
-      mbar_init(&bar_acc2_full[i], 1); mbar_init(&bar_acc2_empty[i], 4);
+      mbar_init(&bar_acc1_full[i], 1); mbar_init(&bar_acc1_empty[i], C::kEpiWarps);
+      mbar_init(&bar_y_full[i], C::kEpiWarps); mbar_init(&bar_y_empty[i], 1);
+      mbar_init(&bar_acc2_full[i], 1); mbar_init(&bar_acc2_empty[i], C::kEpiWarps);
     }
     mbar_init(&bar_const, 1);
     mbar_init(&bar_done, 1);
@@ -331,26 +343,30 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
       mbar_wait(&bar_done, 0, p.err, kDevTimeoutMma);
     }
     __syncwarp();
-  } else if (warp < 6) {
+  } else if (warp < 2 + C::kEpiWarps) {
     // ------------------------------------------------------------ epilogue 1
-    // quadrant q holds TMEM lanes [32q, 32q+32); M=64 -> row block q at lanes
-    // 32q + 16*buf; M=128 -> row blocks 2q, 2q+1 at lanes 32q, 32q+16.
+    // Two warps per TMEM lane quadrant q (warp % 4).  M=64: row block q
+    // (lanes 32q + 16*buf), the two warps split its 64-column chunks;
+    // M=128: row blocks 2q, 2q+1 (lanes 32q, 32q+16), one per warp.
+    // Each thread's shared-memory destinations and twiddles are the same
+    // for every tile and are computed once.
     const uint32_t q = warp & 3u;
-    constexpr int kBlocks = C::M1 / 64;  // row blocks per warp (1 or 2)
-    constexpr int kTwPerBlock = C::NA / 4 > 0 ? C::NA / 4 : 1;
-    float2 tw[kBlocks][kTwPerBlock];
-    // row pair rp = block*8 + lane/4 -> (g1, ks); column complex index
-    // p = 4J + lane%4 -> (c1, a) with a = p % NA in {lane%4 + 4i}.
+    const int h = (int)(warp - 2) >> 2;                 // warp index within its quadrant
+    constexpr int kNC = C::N1 / 64;
+    // M=64: one row block per quadrant, chunks split over EPW warps;
+    // M=128: two row blocks per quadrant, split over EPW warps.
+    constexpr int BPW = (C::M1 == 64) ? 1 : 2 / C::EPW;
+    constexpr int CH = (C::M1 == 64) ? kNC / C::EPW : kNC;
+    const int ch0 = (C::M1 == 64 && C::EPW > 1) ? h * CH : 0;
+    // twiddles w_N^(a ks) of this thread: a = lane%4 + 4i (i < NA/4) per row block
+    constexpr int kTw = C::NA / 4;
+    float2 tw[BPW][kTw];
 #pragma unroll
-    for (int bi = 0; bi < kBlocks; ++bi) {
-      const int block = (C::M1 == 64) ? (int)q : (int)(2 * q + bi);
-      const int rp = block * 8 + (int)(lane >> 2);
-      const int ks = rp % C::NS;
+    for (int bi = 0; bi < BPW; ++bi) {
+      const int block = (C::M1 == 64) ? (int)q : (int)(2 * q) + h * BPW + bi;
+      const int ks = (block * 8 + (int)(lane >> 2)) % C::NS;
 #pragma unroll
-      for (int i = 0; i < kTwPerBlock; ++i) {
-        const int a = (int)(lane & 3u) + 4 * i;
-        tw[bi][i] = p.tw[(a * ks) % C::N];
-      }
+      for (int i = 0; i < kTw; ++i) tw[bi][i] = p.tw[(((int)(lane & 3u) + 4 * i) * ks) % C::N];
     }
     const uint32_t ybase = smem_u32(smem + C::OFF_Y);
     for (int i = 0; i < my_tiles; ++i) {
@@ -361,32 +377,34 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
       tc_fence_after();
       const uint32_t yb = ybase + buf * C::TILE_BYTES;
 #pragma unroll
-      for (int bi = 0; bi < kBlocks; ++bi) {
-        const int block = (C::M1 == 64) ? (int)q : (int)(2 * q + bi);
-        const uint32_t lane_base = (C::M1 == 64) ? 32u * q + 16u * buf : 32u * q + 16u * bi;
-        const uint32_t col_base = (C::M1 == 64) ? 0u : (uint32_t)(buf * C::N1);
+      for (int bi = 0; bi < BPW; ++bi) {
+        const int block = (C::M1 == 64) ? (int)q : (int)(2 * q) + h * BPW + bi;
+        const uint32_t lanes = (C::M1 == 64) ? 32u * q + 16u * buf : 32u * q + 16u * (uint32_t)(h * BPW + bi);
+        const uint32_t cols = (C::M1 == 64) ? 0u : (uint32_t)(buf * C::N1);
         const int rp = block * 8 + (int)(lane >> 2);
         const int g1 = rp / C::NS, ks = rp % C::NS;
 #pragma unroll
-        for (int chunk = 0; chunk < C::N1 / 64; ++chunk) {
+        for (int c = 0; c < CH; ++c) {
           uint32_t r[32];
-          tmem_ld_16x256b_x8(tmem + (lane_base << 16) + col_base + chunk * 64, r);
+          tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c) * 64, r);
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int pidx = 4 * (chunk * 8 + j) + (int)(lane & 3u);
+            const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)(lane & 3u);
             const int c1 = pidx / C::NA, a = pidx % C::NA;
             const float rr = __uint_as_float(r[4 * j + 0]), ri = __uint_as_float(r[4 * j + 1]);
             const float ir = __uint_as_float(r[4 * j + 2]), ii = __uint_as_float(r[4 * j + 3]);
             const float yr = rr - ii, yi = ir + ri;
-            const float2 w = tw[bi][(chunk * 8 + j) % kTwPerBlock];
-            const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
+            // a = lane%4 + 4*((ch0+c)*8 + j) mod NA -> twiddle slot ((ch0+c)*8 + j) mod NA/4,
+            // = (c*8 + j) mod NA/4 because ch0*8 is a multiple of NA/4
+            static_assert((CH * 8) % kTw == 0, "twiddle slot must not depend on the warp's chunk offset");
+            const float2 w = tw[bi][(c * 8 + j) % kTw];
             const int sig = g1 * C::C1 + c1;
             const int g2 = sig / C::C2, c2 = sig % C::C2;
             const uint32_t krow = g2 * C::NA + a;
             const int col = c2 * 2 * C::NS + 2 * ks;
             const uint32_t off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
-            detail::store_complex<C::kIsHalf>(yb + off, zr, zi);
+            detail::store_complex<C::kIsHalf>(yb + off, yr * w.x - yi * w.y, yr * w.y + yi * w.x);
           }
         }
       }
@@ -398,7 +416,11 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
   } else {
     // ------------------------------------------------------------ epilogue 2
     const uint32_t q = warp & 3u;
-    constexpr int kBlocks = C::M2 / 64;
+    const int h = (int)(warp - 2 - C::kEpiWarps) >> 2;
+    constexpr int kNC = C::N2 / 64;
+    constexpr int BPW = (C::M2 == 64) ? 1 : 2 / C::EPW;
+    constexpr int CH = (C::M2 == 64) ? kNC / C::EPW : kNC;
+    const int ch0 = (C::M2 == 64 && C::EPW > 1) ? h * CH : 0;
     for (int i = 0; i < my_tiles; ++i) {
       const long long tile = blockIdx.x + (long long)i * gridDim.x;
       const int buf = i & 1;
@@ -407,20 +429,20 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
       tc_fence_after();
       const long long sig0 = tile * C::T;
 #pragma unroll
-      for (int bi = 0; bi < kBlocks; ++bi) {
-        const int block = (C::M2 == 64) ? (int)q : (int)(2 * q + bi);
-        const uint32_t lane_base = (C::M2 == 64) ? 32u * q + 16u * buf : 32u * q + 16u * bi;
-        const uint32_t col_base = 256u + ((C::M2 == 64) ? 0u : (uint32_t)(buf * C::N2));
+      for (int bi = 0; bi < BPW; ++bi) {
+        const int block = (C::M2 == 64) ? (int)q : (int)(2 * q) + h * BPW + bi;
+        const uint32_t lanes = (C::M2 == 64) ? 32u * q + 16u * buf : 32u * q + 16u * (uint32_t)(h * BPW + bi);
+        const uint32_t cols = 256u + ((C::M2 == 64) ? 0u : (uint32_t)(buf * C::N2));
         const int rp = block * 8 + (int)(lane >> 2);
         const int g2 = rp / C::NA, ka = rp % C::NA;
 #pragma unroll
-        for (int chunk = 0; chunk < C::N2 / 64; ++chunk) {
+        for (int c = 0; c < CH; ++c) {
           uint32_t r[32];
-          tmem_ld_16x256b_x8(tmem + (lane_base << 16) + col_base + chunk * 64, r);
+          tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c) * 64, r);
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int pidx = 4 * (chunk * 8 + j) + (int)(lane & 3u);
+            const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)(lane & 3u);
             const int c2 = pidx / C::NS, ks = pidx % C::NS;
             const float rr = __uint_as_float(r[4 * j + 0]), ri = __uint_as_float(r[4 * j + 1]);
             const float ir = __uint_as_float(r[4 * j + 2]), ii = __uint_as_float(r[4 * j + 3]);
@@ -431,24 +453,24 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
               if constexpr (kEpi == kEpiNatural) {
                 detail::store_out<C::kIsHalf>(p.out, sig * C::N + k, xr, xi);
               } else {
-                const long long img = sig / p.rows, r = sig % p.rows;
+                const long long img = sig / p.rows, rr2 = sig % p.rows;
                 if constexpr (kEpi == kEpiTransposeMul || kEpi == kEpiMulNatural) {
-                  const float2 w = __ldg(p.spec + (((img + p.pair0) % p.chans) * p.rows + r) * C::N + k);
+                  const float2 w = __ldg(p.spec + (((img + p.pair0) % p.chans) * p.rows + rr2) * C::N + k);
                   const float tr = xr * w.x - xi * w.y;
                   xi = xr * w.y + xi * w.x;
                   xr = tr;
                 }
                 if constexpr (kEpi == kEpiTransposeMul || kEpi == kEpiTranspose) {
-                  detail::store_out<C::kIsHalf>(p.out, (img * C::N + k) * p.rows + r, xr, xi);
+                  detail::store_out<C::kIsHalf>(p.out, (img * C::N + k) * p.rows + rr2, xr, xi);
                 } else if constexpr (kEpi == kEpiMulNatural) {
                   detail::store_out<C::kIsHalf>(p.out, sig * C::N + k, xr, xi);
                 } else {
                   // pair p -> images (b, ch), (b+1, ch); fp32 real output
                   const long long pr = img + p.pair0, b = 2 * (pr / p.chans), ch = pr % p.chans;
                   float* y = reinterpret_cast<float*>(p.out);
-                  const long long o = ((b * p.chans + ch) * p.rows + r) * C::N + k;
-                  y[o] = xr;
-                  if (b + 1 < p.nimg_b) y[o + (long long)p.chans * p.rows * C::N] = xi;
+                  const long long oy = ((b * p.chans + ch) * p.rows + rr2) * C::N + k;
+                  y[oy] = xr;
+                  if (b + 1 < p.nimg_b) y[oy + (long long)p.chans * p.rows * C::N] = xi;
                 }
               }
             }
@@ -488,7 +510,7 @@ struct Dft1Cfg {
   static constexpr int SIN = kHalf ? 4 : 2;
   static constexpr uint32_t OFF_B = 0;
   static constexpr uint32_t OFF_IN = B_BYTES;
-  static constexpr uint32_t SMEM_BYTES = OFF_IN + SIN * TILE_BYTES + 1024;
+  static constexpr uint32_t SMEM_BYTES = exclusive_smem(OFF_IN + SIN * TILE_BYTES + 1024);
   static_assert(SMEM_BYTES + 512 <= 232448, "shared memory budget");
   static constexpr int kThreads = 192;                   // producer, MMA, 4 epilogue warps
 };
