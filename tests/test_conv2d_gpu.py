@@ -28,7 +28,13 @@ def reference(x, filt):
 @pytest.mark.gpu
 @pytest.mark.parametrize("B,C,h,w,f,pairs", [(2, 1, 128, 128, 3, None), (3, 2, 128, 256, 5, None),
                                              (1, 3, 256, 128, 31, 1), (4, 2, 512, 512, 31, 3),
-                                             (5, 1, 256, 256, 1, 2)])
+                                             (5, 1, 256, 256, 1, 2),
+                                             # every row length (pair-planar loads: NA = 16 with
+                                             # G1 = 4, 2, 1; NA = 32; NA = 64) and column length
+                                             # (transposed loads with 8, 4, 2 signals per group;
+                                             # 4096 takes the transposing-store path)
+                                             (3, 1, 1024, 2048, 5, None), (2, 2, 2048, 1024, 3, 1),
+                                             (1, 1, 128, 4096, 3, None), (2, 1, 4096, 128, 3, None)])
 def test_conv2d_matches_direct_circular_convolution(cuda, B, C, h, w, f, pairs):
     import torch
 

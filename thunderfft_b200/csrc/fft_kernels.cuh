@@ -83,7 +83,7 @@ struct DType<true> {
 // ---------------------------------------------------------------------------
 // Two-stage configuration per (dtype, N).
 // ---------------------------------------------------------------------------
-template <bool kHalf, int kN>
+template <bool kHalf, int kN, int kVar = 0>
 struct Fft2Shape;
 // float2 / tf32
 template <> struct Fft2Shape<false, 128>  { static constexpr int NS = 8,  NA = 16, G1 = 4, G2 = 2, T = 32, SIN = 4, EPW = 1; };
@@ -99,11 +99,18 @@ template <> struct Fft2Shape<true, 512>   { static constexpr int NS = 16, NA = 3
 template <> struct Fft2Shape<true, 1024>  { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 8, EPW = 1; };
 template <> struct Fft2Shape<true, 2048>  { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 8, EPW = 1; };
 template <> struct Fft2Shape<true, 4096>  { static constexpr int NS = 64, NA = 64, G1 = 1, G2 = 1, T = 1,  SIN = 8, EPW = 1; };
+// float2 / tf32, variant 1: NA = 32 so that one 128-B shared-memory line
+// holds 32 consecutive reals of one input row.  Used by the 2-D convolution's
+// first pass, whose pair-planar tiles keep the two real images in separate
+// 128-B column atoms.
+template <> struct Fft2Shape<false, 128, 1> { static constexpr int NS = 4,  NA = 32, G1 = 8, G2 = 1, T = 32, SIN = 4, EPW = 2; };
+template <> struct Fft2Shape<false, 256, 1> { static constexpr int NS = 8,  NA = 32, G1 = 4, G2 = 1, T = 16, SIN = 4, EPW = 2; };
+template <> struct Fft2Shape<false, 512, 1> { static constexpr int NS = 16, NA = 32, G1 = 2, G2 = 1, T = 8,  SIN = 4, EPW = 2; };
 
-template <bool kHalf, int kN>
+template <bool kHalf, int kN, int kVar = 0>
 struct Fft2Cfg {
   using D = DType<kHalf>;
-  using S = Fft2Shape<kHalf, kN>;
+  using S = Fft2Shape<kHalf, kN, kVar>;
   static constexpr bool kIsHalf = kHalf;
   static constexpr int N = kN, NS = S::NS, NA = S::NA, G1 = S::G1, G2 = S::G2, T = S::T, SIN = S::SIN;
   static_assert(NS * NA == N, "factorization");
@@ -123,7 +130,8 @@ struct Fft2Cfg {
   static_assert(N1 <= 256 && N2 <= 256 && N1 % 16 == 0 && N2 % 16 == 0, "N per MMA");
   static_assert(M1 == 64 || N1 <= 128, "TMEM budget stage 1");
   static_assert(M2 == 64 || N2 <= 128, "TMEM budget stage 2");
-  static_assert(H >= 1 && (H == 1 || G1 == 1), "TMA box needs H or G1 trivial");
+  static_assert(H >= 1, "128-B rows");
+  static constexpr bool kNaturalTma = (H == 1 || G1 == 1);  // natural-layout TMA box exists
   static_assert(K1 % D::kMmaK == 0 && K2 % D::kMmaK == 0, "K");
   // shared-memory map (offsets from a 1024-B aligned base)
   static constexpr uint32_t OFF_A1 = 0;
@@ -148,22 +156,43 @@ struct FftParams {
   long long batch;
   int use_tma;           // input tiles via TMA (aligned input) or thread loads
   uint32_t* err;         // device error word (0 = ok)
-  // Output modes of the stage-2 epilogue used by the 2-D convolution
-  // (kEpi != 0 only; the C2C API uses the natural layout):
-  const float2* spec;    // kEpiMul: out *= spec[((sig/R + pair0) % C)*R + sig%R][k]
+  // Input/output modes used by the 2-D convolution (the C2C API uses the
+  // natural layouts).  Signals come in images of R signals; image pair
+  // pg = pair0 + sig / R belongs to channel pg / ppc and batch images
+  // b = 2 (pg % ppc), b + 1 (channel-major pair order, so consecutive pairs
+  // share one filter spectrum).
+  const float2* spec;    // kEpiMulNatural: out *= spec[ch][sig % R][k]
   long long rows;        // R: signals per image
   long long pair0;       // first image pair of this launch
   int chans;             // C
-  long long nimg_b;      // B (images per channel) for the pair-unpack store
+  long long nimg_b;      // B (images per channel)
+  long long ppc;         // image pairs per channel = ceil(B / 2)
+  int blk_log2;          // kEpiBlocked: log2 of the block width Cb
 };
 
 // Stage-2 epilogue output modes.
 enum EpiMode : int {
   kEpiNatural = 0,        // out[sig][k]
-  kEpiTransposeMul = 1,   // out[img][k][r] (sig = img*R + r), optionally * spectrum
-  kEpiTranspose = 2,      // out[img][k][r]
-  kEpiMulNatural = 3,     // out[sig][k] * spectrum
-  kEpiUnpackPair = 4,     // real fp32 images: Re -> x[b][ch][r][k], Im -> x[b+1][ch][r][k]
+  kEpiBlocked = 2,        // out[img][k / Cb][r][k % Cb] (sig = img*R + r): column-blocked
+  kEpiMulNatural = 3,     // out[sig][k] * spec[ch][r][k]
+  kEpiUnpackPair = 4,     // real fp32 images: Re -> y[b][ch][r][k], Im -> y[b+1][ch][r][k]
+};
+
+// Stage-1 input modes.  All three land in the same MN-major B layout
+// ([128-B column atom][K row][128 B]); they differ in the column order
+// inside a tile, which the stage-1 epilogue undoes:
+//   natural     column = (c * NA + a) * 2 + plane      (interleaved complex rows)
+//   pair planar column = c * 2 NA + plane * NA + a     (two real images, plane = image)
+//   blocked     column = (a * C1 + c) * 2 + plane      (signals are matrix columns)
+// Every TMA box row is one whole 128-B line (a narrower box row would be
+// padded to the swizzle span in shared memory), which is why the pair-planar
+// mode needs NA >= 32 and the column mode reads the column-blocked layout
+// written by kEpiBlocked with Cb = C1: 16 / C1 consecutive rows of a block
+// form one contiguous 128-B line.
+enum InMode : int {
+  kInNatural = 0,         // in[sig][n] complex, by TMA or masked thread loads
+  kInPairPlanar = 1,      // real fp32 x[b][ch][r][n]: signal = row r of images (b, b+1), by TMA
+  kInBlocked = 2,         // in[img][r / C1][n][r % C1] complex: signal r of image img, by TMA
 };
 
 namespace detail {
@@ -207,7 +236,7 @@ __device__ __forceinline__ uint32_t in_tile_offset(int sig, int s, int a) {
 // ---------------------------------------------------------------------------
 // Two-stage kernel
 // ---------------------------------------------------------------------------
-template <class C, int kEpi = kEpiNatural>
+template <class C, int kEpi = kEpiNatural, int kIn = kInNatural>
 __global__ void __launch_bounds__(C::kThreads, 1)
 fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
   using namespace sm100;
@@ -258,7 +287,25 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
       const uint32_t ph = (uint32_t)(i / C::SIN) & 1u;
       if (!mbar_wait_warp(&bar_in_empty[slot], ph ^ 1u, p.err, kDevTimeoutProducer)) break;
       uint8_t* dst = smem + C::OFF_IN + slot * C::TILE_BYTES;
-      if (p.use_tma && tile < full_tiles) {
+      if constexpr (kIn != kInNatural) {
+        // conv2d modes: whole tiles inside one image (R % T == 0, checked by the host)
+        if (lane == 0) {
+          const long long sig0 = tile * C::T;
+          const long long img = sig0 / p.rows, r0 = sig0 - img * p.rows;
+          int c0 = 0, c1 = 0, c2 = 0, c3 = 0, c4 = 0;
+          if constexpr (kIn == kInPairPlanar) {
+            static_assert(C::NA >= 32, "pair-planar rows must fill 128-B lines");
+            const long long pg = p.pair0 + img, ch = pg / p.ppc;
+            c3 = (int)(2 * (pg - ch * p.ppc));                     // {a, s, g | a_hi, plane, row}
+            c4 = (int)(ch * p.rows + r0);
+          } else {
+            c4 = (int)tile;                                        // {line, s, g, a_hi, tile}
+          }
+          mbar_arrive_expect_tx(&bar_in_full[slot], C::TILE_BYTES);
+          tma_load_5d(dst, &tmap_in, &bar_in_full[slot], c0, c1, c2, c3, c4);
+        }
+        __syncwarp();
+      } else if (p.use_tma && tile < full_tiles) {
         if (lane == 0) {
           mbar_arrive_expect_tx(&bar_in_full[slot], C::TILE_BYTES);
           tma_load_5d(dst, &tmap_in, &bar_in_full[slot], 0, 0, 0, 0, (int)tile);
@@ -348,25 +395,40 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
     // Two warps per TMEM lane quadrant q (warp % 4).  M=64: row block q
     // (lanes 32q + 16*buf), the two warps split its 64-column chunks;
     // M=128: row blocks 2q, 2q+1 (lanes 32q, 32q+16), one per warp.
-    // Each thread's shared-memory destinations and twiddles are the same
-    // for every tile and are computed once.
+    // Each thread's twiddles are the same for every tile and are loaded once.
+    static_assert(kIn == kInNatural || !C::kIsHalf, "conv2d input modes are float storage only");
     const uint32_t q = warp & 3u;
     const int h = (int)(warp - 2) >> 2;                 // warp index within its quadrant
+    const int l = (int)(lane & 3u);
     constexpr int kNC = C::N1 / 64;
     // M=64: one row block per quadrant, chunks split over EPW warps;
     // M=128: two row blocks per quadrant, split over EPW warps.
     constexpr int BPW = (C::M1 == 64) ? 1 : 2 / C::EPW;
     constexpr int CH = (C::M1 == 64) ? kNC / C::EPW : kNC;
     const int ch0 = (C::M1 == 64 && C::EPW > 1) ? h * CH : 0;
-    // twiddles w_N^(a ks) of this thread: a = lane%4 + 4i (i < NA/4) per row block
-    constexpr int kTw = C::NA / 4;
+    // A pair-planar signal with NA = 64 spans two chunks (re plane, im plane).
+    constexpr int GC = (kIn == kInPairPlanar && C::NA == 64) ? 2 : 1;
+    static_assert(CH % GC == 0 && (GC == 1 || C::EPW == 1), "chunk groups");
+    // Twiddles w_N^(a ks), one slot per distinct a of this thread:
+    //   natural     a = l + 4 slot                   (slot < NA/4)
+    //   pair planar a = 8 (slot/2) + 2 l + slot%2    (slot < NA/4)
+    //   transposed  a = (4 m + l) / C1, m = ch0*8 + slot*kTq (the warp's chunks only)
+    constexpr int kTq = (kIn == kInBlocked && C::C1 >= 4) ? C::C1 / 4 : 1;
+    constexpr int kTw = (kIn == kInBlocked) ? CH * 8 / kTq : C::NA / 4;
+    static_assert(kIn != kInNatural || (CH * 8) % kTw == 0, "twiddle slot must not depend on the warp's chunk offset");
     float2 tw[BPW][kTw];
 #pragma unroll
     for (int bi = 0; bi < BPW; ++bi) {
       const int block = (C::M1 == 64) ? (int)q : (int)(2 * q) + h * BPW + bi;
       const int ks = (block * 8 + (int)(lane >> 2)) % C::NS;
 #pragma unroll
-      for (int i = 0; i < kTw; ++i) tw[bi][i] = p.tw[(((int)(lane & 3u) + 4 * i) * ks) % C::N];
+      for (int i = 0; i < kTw; ++i) {
+        int a;
+        if constexpr (kIn == kInNatural) a = l + 4 * i;
+        else if constexpr (kIn == kInPairPlanar) a = 8 * (i >> 1) + 2 * l + (i & 1);
+        else a = (4 * (ch0 * 8 + i * kTq) + l) / C::C1;
+        tw[bi][i] = p.tw[(a * ks) % C::N];
+      }
     }
     const uint32_t ybase = smem_u32(smem + C::OFF_Y);
     for (int i = 0; i < my_tiles; ++i) {
@@ -384,21 +446,40 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
         const int rp = block * 8 + (int)(lane >> 2);
         const int g1 = rp / C::NS, ks = rp % C::NS;
 #pragma unroll
-        for (int c = 0; c < CH; ++c) {
-          uint32_t r[32];
-          tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c) * 64, r);
+        for (int c = 0; c < CH; c += GC) {
+          uint32_t r[GC][32];
+#pragma unroll
+          for (int g = 0; g < GC; ++g) tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c + g) * 64, r[g]);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)(lane & 3u);
-            const int c1 = pidx / C::NA, a = pidx % C::NA;
-            const float rr = __uint_as_float(r[4 * j + 0]), ri = __uint_as_float(r[4 * j + 1]);
-            const float ir = __uint_as_float(r[4 * j + 2]), ii = __uint_as_float(r[4 * j + 3]);
+          for (int o = 0; o < 8 * GC; ++o) {
+            // registers of cos*re, cos*im, sin*re, sin*im of this output; (c1, a); twiddle slot
+            int iRR, iRI, iIR, iII, c1, a, slot;
+            if constexpr (kIn == kInPairPlanar) {
+              constexpr int d = C::NA / 8;  // sub-chunks between the re and im planes
+              const int jr = (C::NA == 16) ? ((o >> 1) >> 1) * 4 + ((o >> 1) & 1) : (o >> 1);
+              const int e = o & 1;
+              iRR = 4 * jr + e; iIR = 4 * jr + 2 + e; iRI = 4 * (jr + d) + e; iII = 4 * (jr + d) + 2 + e;
+              const int col = 64 * (ch0 + c) + 8 * jr + 2 * l + e;
+              c1 = col / (2 * C::NA); a = col % (2 * C::NA);
+              slot = 2 * (jr % d) + e;
+            } else {
+              iRR = 4 * o; iRI = 4 * o + 1; iIR = 4 * o + 2; iII = 4 * o + 3;
+              const int pidx = 4 * ((ch0 + c) * 8 + o) + l;
+              if constexpr (kIn == kInNatural) {
+                c1 = pidx / C::NA; a = pidx % C::NA;
+                // a = l + 4*((ch0+c)*8 + o) mod NA -> slot ((ch0+c)*8 + o) mod NA/4
+                // = (c*8 + o) mod NA/4 because ch0*8 is a multiple of NA/4
+                slot = (c * 8 + o) % kTw;
+              } else {
+                a = pidx / C::C1; c1 = pidx % C::C1;
+                slot = (c * 8 + o) / kTq;
+              }
+            }
+            const float rr = __uint_as_float(r[iRR >> 5][iRR & 31]), ri = __uint_as_float(r[iRI >> 5][iRI & 31]);
+            const float ir = __uint_as_float(r[iIR >> 5][iIR & 31]), ii = __uint_as_float(r[iII >> 5][iII & 31]);
             const float yr = rr - ii, yi = ir + ri;
-            // a = lane%4 + 4*((ch0+c)*8 + j) mod NA -> twiddle slot ((ch0+c)*8 + j) mod NA/4,
-            // = (c*8 + j) mod NA/4 because ch0*8 is a multiple of NA/4
-            static_assert((CH * 8) % kTw == 0, "twiddle slot must not depend on the warp's chunk offset");
-            const float2 w = tw[bi][(c * 8 + j) % kTw];
+            const float2 w = tw[bi][slot];
             const int sig = g1 * C::C1 + c1;
             const int g2 = sig / C::C2, c2 = sig % C::C2;
             const uint32_t krow = g2 * C::NA + a;
@@ -428,6 +509,22 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
       if (!mbar_wait_warp(&bar_acc2_full[buf], ph, p.err, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const long long sig0 = tile * C::T;
+      // conv2d modes: all T signals of a tile lie in one image (R % T == 0,
+      // checked by the host), so the image bookkeeping is per tile.
+      long long img = 0, r0 = 0;
+      const float2* spec_t = nullptr;   // kEpiMulNatural: spectrum rows of this tile
+      float* y0 = nullptr;              // kEpiUnpackPair: output rows of images b, b+1
+      float* y1 = nullptr;
+      if constexpr (kEpi != kEpiNatural) {
+        img = sig0 / p.rows;
+        r0 = sig0 - img * p.rows;
+        const long long pg = p.pair0 + img, ch = pg / p.ppc, b = 2 * (pg - ch * p.ppc);
+        if constexpr (kEpi == kEpiMulNatural) spec_t = p.spec + (ch * p.rows + r0) * C::N;
+        if constexpr (kEpi == kEpiUnpackPair) {
+          y0 = reinterpret_cast<float*>(p.out) + ((b * p.chans + ch) * p.rows + r0) * C::N;
+          if (b + 1 < p.nimg_b) y1 = y0 + (long long)p.chans * p.rows * C::N;
+        }
+      }
 #pragma unroll
       for (int bi = 0; bi < BPW; ++bi) {
         const int block = (C::M2 == 64) ? (int)q : (int)(2 * q) + h * BPW + bi;
@@ -446,32 +543,23 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
             const int c2 = pidx / C::NS, ks = pidx % C::NS;
             const float rr = __uint_as_float(r[4 * j + 0]), ri = __uint_as_float(r[4 * j + 1]);
             const float ir = __uint_as_float(r[4 * j + 2]), ii = __uint_as_float(r[4 * j + 3]);
-            const long long sig = sig0 + g2 * C::C2 + c2;
-            if (sig < batch) {
-              const long long k = (long long)C::NS * ka + ks;
+            const int sl = g2 * C::C2 + c2;   // signal within the tile
+            if (sig0 + sl < batch) {
+              const int k = C::NS * ka + ks;
               float xr = rr - ii, xi = ir + ri;
               if constexpr (kEpi == kEpiNatural) {
-                detail::store_out<C::kIsHalf>(p.out, sig * C::N + k, xr, xi);
+                detail::store_out<C::kIsHalf>(p.out, (sig0 + sl) * C::N + k, xr, xi);
+              } else if constexpr (kEpi == kEpiMulNatural) {
+                const float2 w = __ldg(spec_t + sl * C::N + k);
+                detail::store_out<C::kIsHalf>(p.out, (sig0 + sl) * C::N + k, xr * w.x - xi * w.y, xr * w.y + xi * w.x);
+              } else if constexpr (kEpi == kEpiBlocked) {
+                const int lb = p.blk_log2;
+                const long long o = (((img * C::N + k) >> lb) * p.rows + r0 + sl) * (1LL << lb) + (k & ((1 << lb) - 1));
+                detail::store_out<C::kIsHalf>(p.out, o, xr, xi);
               } else {
-                const long long img = sig / p.rows, rr2 = sig % p.rows;
-                if constexpr (kEpi == kEpiTransposeMul || kEpi == kEpiMulNatural) {
-                  const float2 w = __ldg(p.spec + (((img + p.pair0) % p.chans) * p.rows + rr2) * C::N + k);
-                  const float tr = xr * w.x - xi * w.y;
-                  xi = xr * w.y + xi * w.x;
-                  xr = tr;
-                }
-                if constexpr (kEpi == kEpiTransposeMul || kEpi == kEpiTranspose) {
-                  detail::store_out<C::kIsHalf>(p.out, (img * C::N + k) * p.rows + rr2, xr, xi);
-                } else if constexpr (kEpi == kEpiMulNatural) {
-                  detail::store_out<C::kIsHalf>(p.out, sig * C::N + k, xr, xi);
-                } else {
-                  // pair p -> images (b, ch), (b+1, ch); fp32 real output
-                  const long long pr = img + p.pair0, b = 2 * (pr / p.chans), ch = pr % p.chans;
-                  float* y = reinterpret_cast<float*>(p.out);
-                  const long long oy = ((b * p.chans + ch) * p.rows + rr2) * C::N + k;
-                  y[oy] = xr;
-                  if (b + 1 < p.nimg_b) y[oy + (long long)p.chans * p.rows * C::N] = xi;
-                }
+                // fp32 real outputs: Re -> image b, Im -> image b + 1
+                y0[sl * C::N + k] = xr;
+                if (y1) y1[sl * C::N + k] = xi;
               }
             }
           }

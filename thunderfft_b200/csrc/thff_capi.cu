@@ -190,13 +190,17 @@ thff_status upload(const std::vector<uint8_t>& img, void** dst) {
   return THFF_OK;
 }
 
-template <bool kHalf, int kN>
+template <bool kHalf, int kN, int kVar = 0>
 struct ShapeOf {
-  static constexpr int NS = thff::Fft2Shape<kHalf, kN>::NS, NA = thff::Fft2Shape<kHalf, kN>::NA;
-  static constexpr int G1 = thff::Fft2Shape<kHalf, kN>::G1, G2 = thff::Fft2Shape<kHalf, kN>::G2;
+  using S = thff::Fft2Shape<kHalf, kN, kVar>;
+  static constexpr int NS = S::NS, NA = S::NA, G1 = S::G1, G2 = S::G2;
 };
 
-thff_status build_consts(int dtype, int n, bool fwd, Consts* c) {
+// Shape variant 1 (NA = 32, float storage, N <= 512) exists for the 2-D
+// convolution's pair-planar first pass.
+bool has_variant1(int dtype, int n) { return dtype == THFF_F32 && (n == 128 || n == 256 || n == 512); }
+
+thff_status build_consts(int dtype, int n, bool fwd, int var, Consts* c) {
   const bool half = dtype == THFF_F16;
   const int sign = fwd ? -1 : 1;
   thff_status st;
@@ -204,14 +208,17 @@ thff_status build_consts(int dtype, int n, bool fwd, Consts* c) {
     if ((st = upload(build_dft1_matrix(64, sign, half), &c->a1)) != THFF_OK) return st;
   } else {
     int NS = 0, NA = 0, G1 = 0, G2 = 0;
-#define THFF_SHAPE(H, NN)                                                                      \
-  if (half == H && n == NN) {                                                                  \
-    NS = ShapeOf<H, NN>::NS; NA = ShapeOf<H, NN>::NA; G1 = ShapeOf<H, NN>::G1; G2 = ShapeOf<H, NN>::G2; \
+#define THFF_SHAPE(H, NN, V)                                                                   \
+  if (half == H && n == NN && var == V) {                                                      \
+    NS = ShapeOf<H, NN, V>::NS; NA = ShapeOf<H, NN, V>::NA; G1 = ShapeOf<H, NN, V>::G1;        \
+    G2 = ShapeOf<H, NN, V>::G2;                                                                 \
   }
-    THFF_SHAPE(false, 128) THFF_SHAPE(false, 256) THFF_SHAPE(false, 512) THFF_SHAPE(false, 1024)
-    THFF_SHAPE(false, 2048) THFF_SHAPE(false, 4096) THFF_SHAPE(true, 128) THFF_SHAPE(true, 256)
-    THFF_SHAPE(true, 512) THFF_SHAPE(true, 1024) THFF_SHAPE(true, 2048) THFF_SHAPE(true, 4096)
+    THFF_SHAPE(false, 128, 0) THFF_SHAPE(false, 256, 0) THFF_SHAPE(false, 512, 0) THFF_SHAPE(false, 1024, 0)
+    THFF_SHAPE(false, 2048, 0) THFF_SHAPE(false, 4096, 0) THFF_SHAPE(true, 128, 0) THFF_SHAPE(true, 256, 0)
+    THFF_SHAPE(true, 512, 0) THFF_SHAPE(true, 1024, 0) THFF_SHAPE(true, 2048, 0) THFF_SHAPE(true, 4096, 0)
+    THFF_SHAPE(false, 128, 1) THFF_SHAPE(false, 256, 1) THFF_SHAPE(false, 512, 1)
 #undef THFF_SHAPE
+    if (NS == 0) return fail(THFF_INVALID_ARGUMENT, "[ThunderFFT] no such FFT shape");
     if ((st = upload(build_stage_matrix(NS, G1, sign, half), &c->a1)) != THFF_OK) return st;
     if ((st = upload(build_stage_matrix(NA, G2, sign, half), &c->a2)) != THFF_OK) return st;
   }
@@ -224,12 +231,14 @@ thff_status build_consts(int dtype, int n, bool fwd, Consts* c) {
   return upload(tw, &c->tw);
 }
 
-thff_status get_consts(DeviceState& st, int dtype, int n, bool fwd, const Consts** out) {
-  const int key = (dtype * 2 + (fwd ? 1 : 0)) * 8192 + n;
+int consts_key(int dtype, int n, bool fwd, int var) { return ((var * 2 + dtype) * 2 + (fwd ? 1 : 0)) * 8192 + n; }
+
+thff_status get_consts(DeviceState& st, int dtype, int n, bool fwd, const Consts** out, int var = 0) {
+  const int key = consts_key(dtype, n, fwd, var);
   auto it = st.consts.find(key);
   if (it == st.consts.end()) {
     Consts c;
-    thff_status s = build_consts(dtype, n, fwd, &c);
+    thff_status s = build_consts(dtype, n, fwd, var, &c);
     if (s != THFF_OK) return s;
     it = st.consts.emplace(key, c).first;
   }
@@ -267,16 +276,63 @@ thff_status set_smem_attr(DeviceState& st, K kernel, int bytes) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <bool kHalf, int kN, int kEpi = thff::kEpiNatural>
+// Tensor map of a conv2d input mode (float storage).  Both modes deliver the
+// stage-1 tile in the MN-major [128-B column atom][K row][128 B] layout with
+// every box row one whole 128-B line; see thff::InMode for the column order.
+template <class C, int kIn>
+thff_status encode_conv_input(CUtensorMap* map, const void* in, const thff::FftParams& ex, long long batch) {
+  static_assert(!C::kIsHalf, "conv2d input modes are float storage only");
+  uint64_t dims[5], strides[4];
+  uint32_t box[5];
+  if constexpr (kIn == thff::kInPairPlanar) {
+    // x[b][ch][r][n] real; signal c of group g = row r0 + g*C1 + c of images
+    // (b, b+1); n = a + NA s.  Shared memory [c][plane][g | a_hi][s][a].
+    static_assert(C::NA == 32 || (C::NA == 64 && C::G1 == 1), "pair-planar rows must fill 128-B lines");
+    const uint64_t W = C::N, rows = uint64_t(ex.chans) * uint64_t(ex.rows);
+    const uint64_t plane = rows * W * 4;  // image b -> b + 1 of the same channel
+    if constexpr (C::NA == 32) {        // {a, s, g, plane, row}
+      const uint64_t d[5] = {32, uint64_t(C::NS), uint64_t(C::G1), uint64_t(ex.nimg_b), rows};
+      const uint64_t st[4] = {128, uint64_t(C::C1) * W * 4, plane, W * 4};
+      const uint32_t b[5] = {32, uint32_t(C::NS), uint32_t(C::G1), 2, uint32_t(C::C1)};
+      std::memcpy(dims, d, sizeof d); std::memcpy(strides, st, sizeof st); std::memcpy(box, b, sizeof b);
+    } else {                            // {a_lo, s, a_hi, plane, row}
+      const uint64_t d[5] = {32, uint64_t(C::NS), 2, uint64_t(ex.nimg_b), rows};
+      const uint64_t st[4] = {256, 128, plane, W * 4};
+      const uint32_t b[5] = {32, uint32_t(C::NS), 2, 2, uint32_t(C::C1)};
+      std::memcpy(dims, d, sizeof d); std::memcpy(strides, st, sizeof st); std::memcpy(box, b, sizeof b);
+    }
+  } else {
+    // Column-blocked in[blk][n][c] complex, blk = sig / C1 (C1 signals per
+    // block, ex.rows signals per image, blocks consecutive across images);
+    // n = a + NA s, a = a_lo + (16 / C1) a_hi: one 128-B line = 16 / C1
+    // consecutive n of a block.  Shared memory [a_hi][g][s][line].
+    static_assert(16 % C::C1 == 0, "C1 divides a 128-B line");
+    constexpr uint64_t ALO = 16 / C::C1, AHI = C::NA / ALO;
+    const uint64_t blk = uint64_t(C::N) * C::C1 * 8, tiles = uint64_t(batch) / C::T;
+    const uint64_t d[5] = {32, uint64_t(C::NS), uint64_t(C::G1), AHI, tiles};
+    const uint64_t st[4] = {uint64_t(C::NA) * C::C1 * 8, blk, 128, uint64_t(C::G1) * blk};
+    const uint32_t b[5] = {32, uint32_t(C::NS), uint32_t(C::G1), uint32_t(AHI), 1};
+    std::memcpy(dims, d, sizeof d); std::memcpy(strides, st, sizeof st); std::memcpy(box, b, sizeof b);
+  }
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, in, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+}
+
+template <bool kHalf, int kN, int kEpi = thff::kEpiNatural, int kIn = thff::kInNatural, int kVar = 0>
 thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* out, long long batch,
                         cudaStream_t stream, const thff::FftParams* extra = nullptr) {
-  using C = thff::Fft2Cfg<kHalf, kN>;
+  using C = thff::Fft2Cfg<kHalf, kN, kVar>;
   const long long num_tiles = (batch + C::T - 1) / C::T;
   const long long full_tiles = batch / C::T;
-  const bool use_tma = aligned16(in);
+  const bool use_tma = kIn != thff::kInNatural || aligned16(in);
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
-  if (use_tma) {
+  if constexpr (kIn != thff::kInNatural) {
+    if (!extra || extra->rows % C::T != 0 || batch % extra->rows != 0 || !aligned16(in))
+      return fail(THFF_INVALID_ARGUMENT, "[ThunderFFT] conv2d pass: tiles must not straddle images");
+    thff_status s = encode_conv_input<C, kIn>(&map, in, *extra, batch);
+    if (s != THFF_OK) return s;
+  } else if (use_tma) {
+    static_assert(C::kNaturalTma, "natural-layout TMA box needs H or G1 trivial");
     const uint64_t sig_bytes = uint64_t(C::N) * 2 * C::ESZ;
     uint64_t dims[5], strides[4];
     uint32_t box[5];
@@ -293,12 +349,17 @@ thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* 
                            kHalf ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (s != THFF_OK) return s;
   }
+  if constexpr (kEpi != thff::kEpiNatural) {
+    if (!extra || extra->rows % C::T != 0 || extra->ppc < 1)
+      return fail(THFF_INVALID_ARGUMENT, "[ThunderFFT] conv2d pass: tiles must not straddle images");
+  }
   thff::FftParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (extra) p = *extra;
   p.in = in; p.out = out; p.a1 = c.a1; p.a2 = c.a2; p.tw = reinterpret_cast<const float2*>(c.tw);
   p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = st.d_err;
-  p.spec = nullptr; p.rows = 1; p.pair0 = 0; p.chans = 1; p.nimg_b = 0;
-  if (extra) { p.spec = extra->spec; p.rows = extra->rows; p.pair0 = extra->pair0; p.chans = extra->chans; p.nimg_b = extra->nimg_b; }
-  auto kernel = thff::fft2_kernel<C, kEpi>;
+  if (!extra) { p.rows = 1; p.chans = 1; p.ppc = 1; }
+  auto kernel = thff::fft2_kernel<C, kEpi, kIn>;
   thff_status s = set_smem_attr(st, kernel, int(C::SMEM_BYTES));
   if (s != THFF_OK) return s;
   const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
@@ -384,7 +445,7 @@ thff_status launch_conv1d(DeviceState& st, const Consts& c, int lin, const void*
 // Stage matrix + twiddles of the conv kernel: the forward DFT matrix of
 // length L = sqrt(n) (one group) and the forward twiddles of length n.
 thff_status get_conv_consts(DeviceState& st, int n, const Consts** out) {
-  const int key = 7 * 8192 + n;
+  const int key = 15 * 8192 + n;  // outside the range of consts_key
   auto it = st.consts.find(key);
   if (it == st.consts.end()) {
     Consts c;
@@ -404,26 +465,82 @@ thff_status get_conv_consts(DeviceState& st, int n, const Consts** out) {
   return THFF_OK;
 }
 
-// One pass of the 2-D convolution pipeline: length-n C2C transform of
-// `batch` signals with the stage-2 epilogue in mode kEpi.
-template <int kEpi>
-thff_status conv2d_pass(DeviceState& st, int n, bool fwd, const void* in, void* out, long long batch,
-                        const thff::FftParams& extra, cudaStream_t cs) {
-  const Consts* c;
-  thff_status s;
-  {
-    std::lock_guard<std::mutex> lock(g_mutex);
-    if ((s = get_consts(st, THFF_F32, n, fwd, &c)) != THFF_OK) return s;
-  }
+// Signals per stage-1 column group (C1) of the float FFT of length n: the
+// block width of the column-blocked layout that pass reads.
+int conv2d_c1(int n) {
   switch (n) {
-    case 128: return launch_fft2<false, 128, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 256: return launch_fft2<false, 256, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 512: return launch_fft2<false, 512, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 1024: return launch_fft2<false, 1024, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 2048: return launch_fft2<false, 2048, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 4096: return launch_fft2<false, 4096, kEpi>(st, *c, in, out, batch, cs, &extra);
+    case 128: return thff::Fft2Cfg<false, 128>::C1;
+    case 256: return thff::Fft2Cfg<false, 256>::C1;
+    case 512: return thff::Fft2Cfg<false, 512>::C1;
+    case 1024: return thff::Fft2Cfg<false, 1024>::C1;
+    case 2048: return thff::Fft2Cfg<false, 2048>::C1;
+    default: return thff::Fft2Cfg<false, 4096>::C1;
+  }
+}
+
+// One pass of the 2-D convolution pipeline: length-n C2C transform of
+// `batch` signals with input mode kIn and stage-2 epilogue mode kEpi.
+template <int kEpi, int kIn>
+thff_status conv2d_pass(DeviceState& st, const Consts& c, int n, const void* in, void* out, long long batch,
+                        const thff::FftParams& extra, cudaStream_t cs) {
+  // the pair-planar pass uses the NA = 32 shape variant where one exists
+  constexpr int kV = (kIn == thff::kInPairPlanar) ? 1 : 0;
+  switch (n) {
+    case 128: return launch_fft2<false, 128, kEpi, kIn, kV>(st, c, in, out, batch, cs, &extra);
+    case 256: return launch_fft2<false, 256, kEpi, kIn, kV>(st, c, in, out, batch, cs, &extra);
+    case 512: return launch_fft2<false, 512, kEpi, kIn, kV>(st, c, in, out, batch, cs, &extra);
+    case 1024: return launch_fft2<false, 1024, kEpi, kIn>(st, c, in, out, batch, cs, &extra);
+    case 2048: return launch_fft2<false, 2048, kEpi, kIn>(st, c, in, out, batch, cs, &extra);
+    case 4096: return launch_fft2<false, 4096, kEpi, kIn>(st, c, in, out, batch, cs, &extra);
   }
   return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
+}
+
+int ilog2(int v) { int l = 0; while ((1 << l) < v) ++l; return l; }
+
+// The whole 2-D convolution over image pairs [0, pairs) in chunks of `chunk`
+// pairs through the scratch buffers z0, z1 (chunk * h * w complex each):
+//   P1 rows    (length w): real image pair -> complex, FFT     -> z0 [pair][k2 / Ch][r][k2 % Ch]
+//   P2 columns (length h): FFT, x spectrum                      -> z1 [pair][k2][k1]
+//   P3 columns (length h): inverse FFT                          -> z0 [pair][r / Cw][k2][r % Cw]
+//   P4 rows    (length w): inverse FFT, Re/Im -> the two images -> y
+// Ch, Cw = signals per stage-1 column group of the length-h, length-w
+// transforms: P2 and P4 read their signals (columns of the previous pass's
+// output) as whole 128-B lines of the column-blocked layout, and every pass
+// stores rows of at least Cb consecutive complex values.  consts(n, fwd,
+// var, &c) finds the FFT constants of each pass.
+template <class Lookup>
+thff_status conv2d_run(DeviceState& st, Lookup&& consts, long long nimg_b, int chans, int h, int w,
+                       const void* d_x, const void* d_spectra, void* d_y, float2* z0, float2* z1, long long chunk,
+                       cudaStream_t cs) {
+  const Consts *row_f, *col_f, *col_i, *row_i;
+  thff_status s;
+  if ((s = consts(w, true, has_variant1(THFF_F32, w) ? 1 : 0, &row_f)) != THFF_OK ||
+      (s = consts(h, true, 0, &col_f)) != THFF_OK || (s = consts(h, false, 0, &col_i)) != THFF_OK ||
+      (s = consts(w, false, 0, &row_i)) != THFF_OK)
+    return s;
+  const long long ppc = (nimg_b + 1) / 2, pairs = ppc * chans;
+  thff::FftParams ex;
+  std::memset(&ex, 0, sizeof(ex));
+  ex.chans = chans; ex.nimg_b = nimg_b; ex.ppc = ppc; ex.spec = static_cast<const float2*>(d_spectra);
+  for (long long p0 = 0; p0 < pairs; p0 += chunk) {
+    const long long np = (pairs - p0 < chunk) ? pairs - p0 : chunk;
+    ex.pair0 = p0;
+    ex.rows = h;                     // P1: h row signals per image
+    ex.blk_log2 = ilog2(conv2d_c1(h));
+    if ((s = conv2d_pass<thff::kEpiBlocked, thff::kInPairPlanar>(st, *row_f, w, d_x, z0, np * h, ex, cs)) != THFF_OK)
+      return s;
+    ex.rows = w;                     // P2, P3: w column signals per image
+    if ((s = conv2d_pass<thff::kEpiMulNatural, thff::kInBlocked>(st, *col_f, h, z0, z1, np * w, ex, cs)) != THFF_OK)
+      return s;
+    ex.blk_log2 = ilog2(conv2d_c1(w));
+    if ((s = conv2d_pass<thff::kEpiBlocked, thff::kInNatural>(st, *col_i, h, z1, z0, np * w, ex, cs)) != THFF_OK)
+      return s;
+    ex.rows = h;                     // P4: h row signals per image
+    if ((s = conv2d_pass<thff::kEpiUnpackPair, thff::kInBlocked>(st, *row_i, w, z0, d_y, np * h, ex, cs)) != THFF_OK)
+      return s;
+  }
+  return THFF_OK;
 }
 
 bool conv2d_side_ok(int v) { return v == 128 || v == 256 || v == 512 || v == 1024 || v == 2048 || v == 4096; }
@@ -445,31 +562,9 @@ static __device__ __align__(256) unsigned char g_conv2d_scratch[kNoAllocScratchB
 std::map<int, void*> g_noalloc_scratch;  // device -> address of g_conv2d_scratch (under g_mutex)
 
 // Look up FFT constants without building them (building would allocate).
-const Consts* find_consts(DeviceState& st, int dtype, int n, bool fwd) {
-  auto it = st.consts.find((dtype * 2 + (fwd ? 1 : 0)) * 8192 + n);
+const Consts* find_consts(DeviceState& st, int dtype, int n, bool fwd, int var = 0) {
+  auto it = st.consts.find(consts_key(dtype, n, fwd, var));
   return it == st.consts.end() ? nullptr : &it->second;
-}
-
-template <int kEpi>
-thff_status conv2d_pass_noalloc(DeviceState& st, int n, bool fwd, const void* in, void* out, long long batch,
-                                const thff::FftParams& extra, cudaStream_t cs) {
-  const Consts* c;
-  {
-    std::lock_guard<std::mutex> lock(g_mutex);
-    c = find_consts(st, THFF_F32, n, fwd);
-  }
-  if (!c)
-    return fail(THFF_INVALID_ARGUMENT, "thff_conv2d_noalloc: call thff_initialize(THFF_F32, " + std::to_string(n) +
-                                           ") on this device first (this entry point allocates nothing)");
-  switch (n) {
-    case 128: return launch_fft2<false, 128, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 256: return launch_fft2<false, 256, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 512: return launch_fft2<false, 512, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 1024: return launch_fft2<false, 1024, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 2048: return launch_fft2<false, 2048, kEpi>(st, *c, in, out, batch, cs, &extra);
-    case 4096: return launch_fft2<false, 4096, kEpi>(st, *c, in, out, batch, cs, &extra);
-  }
-  return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
 }
 
 thff_status read_device_error(DeviceState& st, cudaStream_t stream) {
@@ -534,6 +629,7 @@ thff_status thff_initialize(int dtype, int n) {
   const Consts* c;
   if ((s = get_consts(*st, dtype, n, true, &c)) != THFF_OK) return s;
   if ((s = get_consts(*st, dtype, n, false, &c)) != THFF_OK) return s;
+  if (has_variant1(dtype, n) && (s = get_consts(*st, dtype, n, true, &c, 1)) != THFF_OK) return s;
   return THFF_OK;
 }
 
@@ -728,32 +824,14 @@ thff_status thff_conv2d_async(int dtype, long long nimg_b, int chans, int h, int
     if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
   }
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  const long long pairs = ((nimg_b + 1) / 2) * chans;
   float2* z0 = static_cast<float2*>(d_workspace);
   float2* z1 = z0 + (size_t)chunk * h * w;
-  const long long hw = (long long)h * w;
-  for (long long p0 = 0; p0 < pairs; p0 += chunk) {
-    const long long np = (pairs - p0 < chunk) ? pairs - p0 : chunk;
-    const long long n4 = np * hw / 4;
-    thff::conv2d_pack_kernel<<<unsigned((n4 + 255) / 256), 256, 0, cs>>>(
-        static_cast<const float*>(d_x), z0, int(nimg_b), chans, int(hw), p0, np);
-    THFF_CUDA(cudaGetLastError(), "conv2d pack launch");
-    thff::FftParams ex;
-    std::memset(&ex, 0, sizeof(ex));
-    ex.chans = chans; ex.pair0 = p0; ex.nimg_b = nimg_b; ex.spec = static_cast<const float2*>(d_spectra);
-    // rows forward, written transposed: z1[p][k2][r]
-    ex.rows = h;
-    if ((s = conv2d_pass<thff::kEpiTranspose>(*st, w, true, z0, z1, np * h, ex, cs)) != THFF_OK) return s;
-    // columns forward, times the spectrum: z0[p][k2][k1]
-    ex.rows = w;
-    if ((s = conv2d_pass<thff::kEpiMulNatural>(*st, h, true, z1, z0, np * w, ex, cs)) != THFF_OK) return s;
-    // columns inverse, written transposed back: z1[p][r][k2]
-    if ((s = conv2d_pass<thff::kEpiTranspose>(*st, h, false, z0, z1, np * w, ex, cs)) != THFF_OK) return s;
-    // rows inverse, real/imaginary parts to the two images of each pair
-    ex.rows = h;
-    if ((s = conv2d_pass<thff::kEpiUnpackPair>(*st, w, false, z1, d_y, np * h, ex, cs)) != THFF_OK) return s;
-  }
-  return THFF_OK;
+  auto consts = [st](int n, bool fwd, int var, const Consts** c) -> thff_status {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    return get_consts(*st, THFF_F32, n, fwd, c, var);
+  };
+  return conv2d_run(*st, consts, nimg_b, chans, h, w, d_x, d_spectra, d_y, z0, z1, chunk,
+                    reinterpret_cast<cudaStream_t>(stream));
 }
 
 thff_status thff_conv2d(int dtype, long long nimg_b, int chans, int h, int w, const void* d_x, const void* d_spectra,
@@ -799,32 +877,23 @@ thff_status thff_conv2d_noalloc(int dtype, long long nimg_b, int chans, int h, i
     }
     scratch = sc->second;
   }
-  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
   const long long chunk = kNoAllocScratchBytes / per_pair;
-  const long long pairs = ((nimg_b + 1) / 2) * chans;
   float2* z0 = static_cast<float2*>(scratch);
   float2* z1 = z0 + (size_t)chunk * h * w;
-  const long long hw = (long long)h * w;
-  // Every pass below writes its whole output region before the next pass
-  // reads it, so nothing left in the scratch by an earlier call is read.
-  for (long long p0 = 0; p0 < pairs; p0 += chunk) {
-    const long long np = (pairs - p0 < chunk) ? pairs - p0 : chunk;
-    const long long n4 = np * hw / 4;
-    thff::conv2d_pack_kernel<<<unsigned((n4 + 255) / 256), 256, 0, cs>>>(
-        static_cast<const float*>(d_x), z0, int(nimg_b), chans, int(hw), p0, np);
-    THFF_CUDA(cudaGetLastError(), "conv2d pack launch");
-    thff::FftParams ex;
-    std::memset(&ex, 0, sizeof(ex));
-    ex.chans = chans; ex.pair0 = p0; ex.nimg_b = nimg_b; ex.spec = static_cast<const float2*>(d_spectra);
-    ex.rows = h;
-    if ((s = conv2d_pass_noalloc<thff::kEpiTranspose>(*st, w, true, z0, z1, np * h, ex, cs)) != THFF_OK) return s;
-    ex.rows = w;
-    if ((s = conv2d_pass_noalloc<thff::kEpiMulNatural>(*st, h, true, z1, z0, np * w, ex, cs)) != THFF_OK) return s;
-    if ((s = conv2d_pass_noalloc<thff::kEpiTranspose>(*st, h, false, z0, z1, np * w, ex, cs)) != THFF_OK) return s;
-    ex.rows = h;
-    if ((s = conv2d_pass_noalloc<thff::kEpiUnpackPair>(*st, w, false, z1, d_y, np * h, ex, cs)) != THFF_OK) return s;
-  }
-  return THFF_OK;
+  // Constants are looked up, never built (building allocates).  Every pass
+  // writes its whole output region before the next pass reads it, so nothing
+  // left in the scratch by an earlier call is read.
+  auto consts = [st](int n, bool fwd, int var, const Consts** c) -> thff_status {
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      *c = find_consts(*st, THFF_F32, n, fwd, var);
+    }
+    if (*c) return THFF_OK;
+    return fail(THFF_INVALID_ARGUMENT, "thff_conv2d_noalloc: call thff_initialize(THFF_F32, " + std::to_string(n) +
+                                           ") on this device first (this entry point allocates nothing)");
+  };
+  return conv2d_run(*st, consts, nimg_b, chans, h, w, d_x, d_spectra, d_y, z0, z1, chunk,
+                    reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"
