@@ -83,11 +83,165 @@ __device__ __forceinline__ uint32_t acc_addr(uint32_t tmem, int s, uint32_t q, i
   }
 }
 
-// Load the 2L planar columns of complex signal c (re plane then im plane).
-template <class C>
-__device__ __forceinline__ void load_planar(uint32_t addr, int c, uint32_t (&re)[C::L / 2], uint32_t (&im)[C::L / 2]);
 
 }  // namespace detail
+
+// One epilogue pass of stage S (0..3) on tile j of the conv1d kernel (see
+// the kernel for the thread <-> data mapping and the per-thread constants).
+template <class C, int S>
+__device__ __forceinline__ bool conv1d_epilogue(const Conv1dParams& p, int j, uint32_t tmem, uint8_t* bbuf,
+                                            uint64_t* bar_d_full, uint64_t* bar_d_empty, uint64_t* bar_b_full,
+                                            uint64_t* bar_b_empty, uint32_t q, uint32_t lane, int l4,
+                                            const int (&ksv)[C::kBlocks],
+                                            const float4 (&cst)[C::kBlocks][C::L / 8],
+                                            const uint32_t (&ba)[C::kBlocks][2],
+                                            const uint32_t (&bb)[C::kBlocks][4]) {
+  using namespace sm100;
+  constexpr int kU = C::L / 8;
+  constexpr int kB = C::kBlocks;
+  constexpr bool kInverse = S >= 2;
+  const long long batch = p.batch;
+  const uint32_t ph = (uint32_t)j & 1u;
+  if (!mbar_wait_warp(&bar_d_full[S], ph, p.err, kDevTimeoutEpilogue)) return false;
+  if (S < 3 && !mbar_wait_warp(&bar_b_empty[S], ph ^ 1u, p.err, kDevTimeoutEpilogue)) return false;
+  tc_fence_after();
+  const long long tile = blockIdx.x + (long long)j * gridDim.x;
+  const uint32_t bdst = smem_u32(bbuf + (S < 3 ? S : 0) * C::TILE_BYTES);
+#pragma unroll
+  for (int bi = 0; bi < kB; ++bi) {
+    const uint32_t abase = detail::acc_addr<C>(tmem, S, q, bi);
+#pragma unroll
+    for (int c = 0; c < C::TC; ++c) {
+      // planar columns of complex signal c: re plane [c*2L, c*2L+L), im plane [c*2L+L, c*2L+2L)
+      uint32_t vr[C::L / 2], vi[C::L / 2];
+      if constexpr (C::L == 64) {
+        tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L), vr);
+        tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L + C::L), vi);
+        tmem_wait_ld();
+      } else {
+        uint32_t t0[32];
+        tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L), t0);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { vr[i] = t0[i]; vi[i] = t0[16 + i]; }
+      }
+      // column-atom offsets of this signal's re / im planes
+      const uint32_t atom_re = (uint32_t)((c * 2 * C::L) / C::E) * C::LBO;
+      const uint32_t atom_im = (uint32_t)((c * 2 * C::L + C::L) / C::E) * C::LBO;
+      float* yre = nullptr;
+      float* yim = nullptr;
+      if constexpr (S == 3) {
+        const long long sig0 = tile * (2LL * C::TC) + 2 * c;
+        float* row = p.y + sig0 * C::N + C::L * ksv[bi] + 2 * l4;
+        if (sig0 < batch) yre = row;
+        if (sig0 + 1 < batch) yim = row + C::N;
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        float yr[2], yi[2];
+#pragma unroll
+        for (int o = 0; o < 2; ++o) {
+          const float RR = __uint_as_float(vr[4 * u + o]), IR = __uint_as_float(vr[4 * u + 2 + o]);
+          const float RI = __uint_as_float(vi[4 * u + o]), II = __uint_as_float(vi[4 * u + 2 + o]);
+          yr[o] = kInverse ? RR + II : RR - II;
+          yi[o] = kInverse ? RI - IR : IR + RI;
+        }
+        const float4 k4 = cst[bi][u];
+        if constexpr (S == 0 || S == 2) {
+          // twiddle, then B(S+2)[K row = i0 + o][c, plane, ks]
+#pragma unroll
+          for (int o = 0; o < 2; ++o) {
+            const float wx = o ? k4.z : k4.x;
+            const float wy = kInverse ? -(o ? k4.w : k4.y) : (o ? k4.w : k4.y);
+            const float zr = yr[o] * wx - yi[o] * wy, zi = yr[o] * wy + yi[o] * wx;
+            const uint32_t off = 1024u * (uint32_t)u + ba[bi][o];
+            st_shared_b32(bdst + atom_re + off, __float_as_uint(round_tf32(zr)));
+            st_shared_b32(bdst + atom_im + off, __float_as_uint(round_tf32(zi)));
+          }
+        } else if constexpr (S == 1) {
+          // X[L ka + i0 + o] * H, written as the inverse's input B3[K row = ka][c, plane, i0 + o]
+          const float z0r = yr[0] * k4.x - yi[0] * k4.y, z0i = yr[0] * k4.y + yi[0] * k4.x;
+          const float z1r = yr[1] * k4.z - yi[1] * k4.w, z1i = yr[1] * k4.w + yi[1] * k4.z;
+          const uint32_t off = (uint32_t)(u / 4) * C::LBO + bb[bi][u % 4];
+          st_shared_v2(bdst + atom_re + off, round_tf32(z0r), round_tf32(z1r));
+          st_shared_v2(bdst + atom_im + off, round_tf32(z0i), round_tf32(z1i));
+        } else {
+          // outputs m = L ks + i0 + o: re -> signal 2c, im -> signal 2c+1
+          if (yre) *reinterpret_cast<float2*>(yre + 8 * u) = make_float2(yr[0], yr[1]);
+          if (yim) *reinterpret_cast<float2*>(yim + 8 * u) = make_float2(yi[0], yi[1]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  if (S < 3) fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    mbar_arrive(&bar_d_empty[S]);
+    if (S < 3) mbar_arrive(&bar_b_full[S]);
+  }
+  return true;
+}
+
+// Epilogue warps of the conv1d kernel: group A (kGroupA, warps 2-5) runs E1
+// and E3, group B (warps 6-9) runs E2 and E4, each over all rounds.  The two
+// groups keep different per-thread constants, so they are separate
+// instantiations (the registers of one never hold the other's).
+template <class C, bool kGroupA>
+__device__ __forceinline__ void conv1d_epilogue_group(const Conv1dParams& p, int T, uint32_t tmem, uint8_t* bbuf,
+                                                      uint64_t* bar_d_full, uint64_t* bar_d_empty,
+                                                      uint64_t* bar_b_full, uint64_t* bar_b_empty, uint32_t warp,
+                                                      uint32_t lane) {
+  const uint32_t q = warp & 3u;
+  const int l4 = (int)(lane & 3u);
+  constexpr int kU = C::L / 8;
+  constexpr int kB = C::kBlocks;
+  int ksv[kB];
+#pragma unroll
+  for (int bi = 0; bi < kB; ++bi) ksv[bi] = ((C::M == 64) ? (int)q : (int)(2 * q + bi)) * 8 + (int)(lane >> 2);
+  // group A: forward twiddles w_N^-(a ks) of its pairs (inverse = conjugate);
+  // group B: spectrum values H[L ka + i0 + o] (ka = ks) as float4 pairs.
+  float4 cst[kB][kU];
+  // group A stores (E1/E3): B(s+2)[K row 8u + 2 l4 + o][col base + ks]
+  //   = col-atom offset + 1024 u + ba[bi][o]
+  // group B stores (E2): B3[K row ks][col base + 8u + 2 l4] (v2)
+  //   = col-atom offset + LBO (u / 4) + bb[bi][u % 4]
+  uint32_t ba[kB][2], bb[kB][4];
+#pragma unroll
+  for (int bi = 0; bi < kB; ++bi) {
+    const int ks = ksv[bi];
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+      const uint32_t kr = (uint32_t)(2 * l4 + o);
+      ba[bi][o] = (uint32_t)(ks / C::E) * C::LBO + kr * 128u + ((uint32_t)((ks % C::E) * 4) ^ ((kr & 3u) << 5));
+    }
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+      bb[bi][v] = (uint32_t)ks * 128u + 8u * (uint32_t)l4 + ((uint32_t)(v ^ (ks & 3)) << 5);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int i0 = 8 * u + 2 * l4;
+      if constexpr (kGroupA) {
+        const float2 w0 = p.tw[(i0 * ks) % C::N], w1 = p.tw[((i0 + 1) * ks) % C::N];
+        cst[bi][u] = make_float4(w0.x, w0.y, w1.x, w1.y);
+      } else {
+        cst[bi][u] = __ldg(reinterpret_cast<const float4*>(p.spec + C::L * ks + i0));
+      }
+    }
+  }
+
+  for (int r = 0; r < T + 3; ++r) {
+    bool ok = true;
+    if constexpr (kGroupA) {
+      if (r < T) ok = conv1d_epilogue<C, 0>(p, r, tmem, bbuf, bar_d_full, bar_d_empty, bar_b_full, bar_b_empty, q, lane, l4, ksv, cst, ba, bb);
+      if (ok && r >= 2 && r - 2 < T) ok = conv1d_epilogue<C, 2>(p, r - 2, tmem, bbuf, bar_d_full, bar_d_empty, bar_b_full, bar_b_empty, q, lane, l4, ksv, cst, ba, bb);
+    } else {
+      if (r >= 1 && r - 1 < T) ok = conv1d_epilogue<C, 1>(p, r - 1, tmem, bbuf, bar_d_full, bar_d_empty, bar_b_full, bar_b_empty, q, lane, l4, ksv, cst, ba, bb);
+      if (ok && r >= 3) ok = conv1d_epilogue<C, 3>(p, r - 3, tmem, bbuf, bar_d_full, bar_d_empty, bar_b_full, bar_b_empty, q, lane, l4, ksv, cst, ba, bb);
+    }
+    if (!ok) break;
+  }
+}
 
 template <class C>
 __global__ void __launch_bounds__(C::kThreads, 1)
@@ -189,111 +343,13 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
     // ------------------------------------------------------------ epilogues
     // group A (warps 2-5): E1 (D0 -> B2) and E3 (D2 -> B4)
     // group B (warps 6-9): E2 (D1 -> *H -> B3) and E4 (D3 -> y)
-    const bool groupA = warp < 6;
-    const uint32_t q = warp & 3u;
-    const int l4 = (int)(lane & 3u);
-    // Each thread owns index pairs (i0, i0+1), i0 = 8u + 2*l4, u < L/8, of
-    // row pair ks = block*8 + lane/4.  Group A keeps the forward twiddles
-    // w_N^-(a ks) of its pairs in registers (inverse = conjugate).
-    constexpr int kU = C::L / 8;
-    float2 tw[C::kBlocks][kU][2];
-#pragma unroll
-    for (int bi = 0; bi < C::kBlocks; ++bi) {
-      const int ks = (C::M == 64 ? (int)q : (int)(2 * q + bi)) * 8 + (int)(lane >> 2);
-#pragma unroll
-      for (int u = 0; u < kU; ++u)
-#pragma unroll
-        for (int o = 0; o < 2; ++o) tw[bi][u][o] = groupA ? p.tw[((8 * u + 2 * l4 + o) * ks) % C::N] : make_float2(0.f, 0.f);
-    }
-    const int first = groupA ? 0 : 1;      // E1/E3 or E2/E4
-    for (int r = 0; r < T + 3; ++r) {
-      bool ok = true;
-#pragma unroll 1
-      for (int which = 0; which < 2; ++which) {
-        const int s = first + 2 * which;   // accumulator index 0..3
-        const int j = r - s;               // tile of this stage in round r
-        if (j < 0 || j >= T) continue;
-        const uint32_t ph = (uint32_t)j & 1u;
-        if (!mbar_wait_warp(&bar_d_full[s], ph, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
-        if (s < 3 && !mbar_wait_warp(&bar_b_empty[s], ph ^ 1u, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
-        tc_fence_after();
-        const bool inverse = s >= 2;
-        const long long tile = blockIdx.x + (long long)j * gridDim.x;
-        const uint32_t bdst = smem_u32(bbuf + (s < 3 ? s : 0) * C::TILE_BYTES);
-#pragma unroll
-        for (int bi = 0; bi < C::kBlocks; ++bi) {
-          const int blk = (C::M == 64) ? (int)q : (int)(2 * q + bi);
-          const int ks = blk * 8 + (int)(lane >> 2);  // row pair: stage output index
-          const uint32_t abase = detail::acc_addr<C>(tmem, s, q, bi);
-#pragma unroll 1
-          for (int c = 0; c < C::TC; ++c) {
-            // planar columns of signal c: re plane [c*2L, c*2L+L), im plane [c*2L+L, c*2L+2L)
-            uint32_t vr[C::L / 2], vi[C::L / 2];
-            if constexpr (C::L == 64) {
-              uint32_t t0[32], t1[32];
-              tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L), t0);
-              tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L + C::L), t1);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) { vr[i] = t0[i]; vi[i] = t1[i]; }
-            } else {
-              uint32_t t0[32];
-              tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L), t0);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 16; ++i) { vr[i] = t0[i]; vi[i] = t0[16 + i]; }
-            }
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-              float yr[2], yi[2];
-#pragma unroll
-              for (int o = 0; o < 2; ++o) {
-                const float RR = __uint_as_float(vr[4 * u + o]), IR = __uint_as_float(vr[4 * u + 2 + o]);
-                const float RI = __uint_as_float(vi[4 * u + o]), II = __uint_as_float(vi[4 * u + 2 + o]);
-                yr[o] = inverse ? RR + II : RR - II;
-                yi[o] = inverse ? RI - IR : IR + RI;
-              }
-              const int i0 = 8 * u + 2 * l4;  // input index pair of this stage
-              if (s == 0 || s == 2) {
-                // twiddle, then B(s+2)[K row = i][c, plane, ks]
-#pragma unroll
-                for (int o = 0; o < 2; ++o) {
-                  const float2 w = tw[bi][u][o];
-                  const float wy = inverse ? -w.y : w.y;
-                  const float zr = yr[o] * w.x - yi[o] * wy, zi = yr[o] * wy + yi[o] * w.x;
-                  st_shared_b32(bdst + detail::planar_off<C>(i0 + o, c * 2 * C::L + ks), __float_as_uint(round_tf32(zr)));
-                  st_shared_b32(bdst + detail::planar_off<C>(i0 + o, c * 2 * C::L + C::L + ks), __float_as_uint(round_tf32(zi)));
-                }
-              } else if (s == 1) {
-                // X[k], k = L*ks + i (ks = ka here): multiply by H, write the
-                // inverse's input B3[K row = ks][c, plane, i]
-                const float4 h = __ldg(reinterpret_cast<const float4*>(p.spec + C::L * ks + i0));
-                const float z0r = yr[0] * h.x - yi[0] * h.y, z0i = yr[0] * h.y + yi[0] * h.x;
-                const float z1r = yr[1] * h.z - yi[1] * h.w, z1i = yr[1] * h.w + yi[1] * h.z;
-                st_shared_v2(bdst + detail::planar_off<C>(ks, c * 2 * C::L + i0), round_tf32(z0r), round_tf32(z1r));
-                st_shared_v2(bdst + detail::planar_off<C>(ks, c * 2 * C::L + C::L + i0), round_tf32(z0i), round_tf32(z1i));
-              } else {
-                // output m = L*ks + i: re -> signal 2c, im -> signal 2c+1
-                const long long sig0 = tile * (2LL * C::TC) + 2 * c;
-                const long long m = (long long)C::L * ks + i0;
-                if (sig0 < batch)
-                  *reinterpret_cast<float2*>(p.y + sig0 * C::N + m) = make_float2(yr[0], yr[1]);
-                if (sig0 + 1 < batch)
-                  *reinterpret_cast<float2*>(p.y + (sig0 + 1) * C::N + m) = make_float2(yi[0], yi[1]);
-              }
-            }
-          }
-        }
-        tc_fence_before();
-        if (s < 3) fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&bar_d_empty[s]);
-          if (s < 3) mbar_arrive(&bar_b_full[s]);
-        }
-      }
-      if (!ok) break;
-    }
+    // Thread (q = warp % 4, lane) owns, per 16-row block bi, the row pair
+    // ks = block*8 + lane/4 and the index pairs (i0, i0+1), i0 = 8u + 2*l4,
+    // u < L/8.  Everything that depends only on (ks, l4) — twiddles or
+    // spectrum values, shared-memory bases with the swizzle folded in — is
+    // computed once; per element only compile-time offsets remain.
+    if (warp < 6) conv1d_epilogue_group<C, true>(p, T, tmem, bbuf, bar_d_full, bar_d_empty, bar_b_full, bar_b_empty, warp, lane);
+    else conv1d_epilogue_group<C, false>(p, T, tmem, bbuf, bar_d_full, bar_d_empty, bar_b_full, bar_b_empty, warp, lane);
   }
 
   tc_fence_before();
