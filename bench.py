@@ -157,6 +157,105 @@ def cpu_baseline(seconds: float = 12.0, sample_batch: int = 2048):
                       f"{dt:.1f} s on {threads} threads"}
 
 
+SWEEP_N = (64, 128, 256, 512, 1024, 2048, 4096)
+
+
+def run_sweep(args):
+    """Per-size table (not the contract line): every N and storage type in both
+    directions at BASELINE config 3's batch 2^26/N (divided by --sweep-scale),
+    plus config 3's masked partial batch (batch - 7) for half2, then the
+    conv1d (config 4) and conv2d (config 5) kernels.  Event-timed on one GPU,
+    inputs resident in HBM, each launch streaming buffers larger than L2 at
+    scale 1.  Prints a markdown table."""
+    import torch
+    import thunderfft_b200 as tf
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_kind = measured_peaks()
+    steps, warm = max(args.steps, 1), args.warmup
+
+    def timed(fn):
+        for _ in range(warm):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        tf.sync_check(stream)
+        return e0.elapsed_time(e1) / steps * 1e3  # us per call
+
+    print(f"| storage | N | batch | direction | us / launch | GB/s | of {peak_kind} peak ({peak:.0f} GB/s) | rel. L2 (round trip) |")
+    print("|---|---|---|---|---|---|---|---|")
+    g = torch.Generator(device=dev)
+    g.manual_seed(33)
+    only = args.sweep_only
+    for dtype in (("float", "half") if only in ("all", "fft") else ()):
+        esz = 8 if dtype == "float" else 4
+        for n in SWEEP_N:
+            full = (1 << 26) // n // args.sweep_scale
+            for b in ((full, full - 7) if dtype == "half" else (full,)):
+                if dtype == "float":
+                    x = torch.complex(torch.rand(b, n, device=dev, generator=g) * 2 - 1,
+                                      torch.rand(b, n, device=dev, generator=g) * 2 - 1).contiguous()
+                else:
+                    x = (torch.rand(b, n, 2, device=dev, generator=g) - 0.5).half()
+                y, z = torch.empty_like(x), torch.empty_like(x)
+                tf.ThunderFFTInitialize(dtype, n)
+                us_f = timed(lambda: tf.c2c_async(dtype, n, True, x, y, b, stream))
+                us_i = timed(lambda: tf.c2c_async(dtype, n, False, y, z, b, stream))
+                xs = torch.view_as_real(x[:256]) if x.is_complex() else x[:256].float()
+                zs = torch.view_as_real(z[:256]) if z.is_complex() else z[:256].float()
+                err = float(((zs / n - xs).pow(2).sum() / xs.pow(2).sum()).sqrt())
+                for d, us in (("fwd", us_f), ("inv", us_i)):
+                    gbs = 2 * n * b * esz / us / 1e3
+                    print(f"| {'float2' if dtype == 'float' else 'half2'} | {n} | {b} | {d} | {us:.1f} | {gbs:.0f} | "
+                          f"{gbs / peak:.3f} | {err:.2e} |", flush=True)
+                del x, y, z
+                torch.cuda.empty_cache()
+    if args.no_conv or only == "fft":
+        return 0
+    if only in ("all", "conv1d"):
+        sweep_conv1d(args, tf, dev, g, stream, timed, peak)
+    if only in ("all", "conv2d"):
+        sweep_conv2d(args, tf, dev, g, stream, timed, peak)
+    return 0
+
+
+def sweep_conv1d(args, tf, dev, g, stream, timed, peak):
+    """conv1d row of the sweep: BASELINE config 4 (batch / --sweep-scale)."""
+    import torch
+
+    B1, lin, taps, n1 = 16384 // args.sweep_scale, 3072, 1025, 4096
+    xs = torch.randn(B1, lin, device=dev, generator=g)
+    hs = torch.randn(taps, device=dev, generator=g)
+    spec = tf.conv1d_filter_spectrum(hs, n1)
+    ys = torch.empty(B1, n1, device=dev)
+    us = timed(lambda: tf.conv1d(xs, spec, n1, out=ys, stream=stream, sync=False))
+    alg = B1 * (lin + n1) * 4
+    print(f"| conv1d fp32 (config 4) | {n1} | {B1} x {lin} | fwd*H*inv | {us:.1f} | {alg / us / 1e3:.0f} | "
+          f"{alg / us / 1e3 / peak:.3f} | |", flush=True)
+
+
+def sweep_conv2d(args, tf, dev, g, stream, timed, peak):
+    """conv2d row of the sweep: BASELINE config 5 (batch / --sweep-scale)."""
+    import torch
+
+    B2, C2, hw, f = 64 // args.sweep_scale, 32, 512, 31
+    xi = torch.randn(B2, C2, hw, hw, device=dev, generator=g)
+    fi = torch.randn(C2, f, f, device=dev, generator=g)
+    sp = tf.conv2d_filter_spectra(fi, hw, hw)
+    ws = tf.conv2d_workspace(hw, hw, (B2 // 2) * C2)
+    yi = torch.empty_like(xi)
+    us = timed(lambda: tf.conv2d(xi, sp, ws, out=yi, stream=stream, sync=False))
+    alg = 2 * xi.numel() * 4
+    print(f"| conv2d fp32 (config 5) | {hw}x{hw} | {B2} x {C2} | fwd*H*inv | {us:.1f} | {alg / us / 1e3:.0f} | "
+          f"{alg / us / 1e3 / peak:.3f} | |", flush=True)
+
+
 def dist_setup(gpus: int):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -209,10 +308,18 @@ def main():
     ap.add_argument("--batch", type=int, default=65536, help="signals per GPU")
     ap.add_argument("--dtype", default="float", choices=["float", "half"])
     ap.add_argument("--no-extras", action="store_true", help="skip cuFFT, e2e and CPU legs (profiling)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="print the per-size table (all N, both storage types, conv kernels) instead of the JSON line")
+    ap.add_argument("--sweep-scale", type=int, default=1, help="divide the sweep's batches by this (profiling)")
+    ap.add_argument("--no-conv", action="store_true", help="sweep: skip the conv1d / conv2d rows")
+    ap.add_argument("--sweep-only", default="all", choices=["all", "fft", "conv1d", "conv2d"],
+                    help="sweep: run only these rows (profiling one kernel)")
     args = ap.parse_args()
     configure(args.n, args.batch, args.dtype)
     if args.no_extras:
         args.no_cpu_baseline = True
+    if args.sweep:
+        return run_sweep(args)
     if args.impl == "reference":
         return run_reference(args)
 

@@ -107,70 +107,81 @@ __device__ __forceinline__ bool conv1d_epilogue(const Conv1dParams& p, int j, ui
   tc_fence_after();
   const long long tile = blockIdx.x + (long long)j * gridDim.x;
   const uint32_t bdst = smem_u32(bbuf + (S < 3 ? S : 0) * C::TILE_BYTES);
+  // The accumulator is read in four pieces of 32 registers (re and im planes
+  // of four index pairs u): L = 64 -> (block, half of the u range), L = 32 ->
+  // (signal c).  The load of piece i+1 is in flight while piece i is
+  // processed (tcgen05.wait::ld waits for all outstanding loads).
+  static_assert(kB * C::TC * (C::L / 32) == 4, "four accumulator pieces per stage");
+  auto load_piece = [&](int pc, uint32_t (&v)[32]) {
+    if constexpr (C::L == 64) {
+      const uint32_t a = detail::acc_addr<C>(tmem, S, q, pc >> 1) + 32u * (uint32_t)(pc & 1);
+      tmem_ld_16x256b_x4(a, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+      tmem_ld_16x256b_x4(a + C::L, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+    } else {
+      tmem_ld_16x256b_x8(detail::acc_addr<C>(tmem, S, q, 0) + (uint32_t)(pc * 2 * C::L), v);
+    }
+  };
+  uint32_t vbuf[2][32];
+  load_piece(0, vbuf[0]);
+  tmem_wait_ld();
+  tmem_regs_ready(vbuf[0]);
 #pragma unroll
-  for (int bi = 0; bi < kB; ++bi) {
-    const uint32_t abase = detail::acc_addr<C>(tmem, S, q, bi);
+  for (int pc = 0; pc < 4; ++pc) {
+    if (pc < 3) load_piece(pc + 1, vbuf[(pc + 1) & 1]);
+    const uint32_t (&v)[32] = vbuf[pc & 1];   // v[0..15]: re plane, v[16..31]: im plane
+    const int bi = (C::L == 64) ? (pc >> 1) : 0;
+    const int c = (C::L == 64) ? 0 : pc;
+    const int u0 = (C::L == 64) ? 4 * (pc & 1) : 0;
+    // column-atom offsets of signal c's re / im planes
+    const uint32_t atom_re = (uint32_t)((c * 2 * C::L) / C::E) * C::LBO;
+    const uint32_t atom_im = (uint32_t)((c * 2 * C::L + C::L) / C::E) * C::LBO;
+    float* yre = nullptr;
+    float* yim = nullptr;
+    if constexpr (S == 3) {
+      const long long sig0 = tile * (2LL * C::TC) + 2 * c;
+      float* row = p.y + sig0 * C::N + C::L * ksv[bi] + 2 * l4;
+      if (sig0 < batch) yre = row;
+      if (sig0 + 1 < batch) yim = row + C::N;
+    }
 #pragma unroll
-    for (int c = 0; c < C::TC; ++c) {
-      // planar columns of complex signal c: re plane [c*2L, c*2L+L), im plane [c*2L+L, c*2L+2L)
-      uint32_t vr[C::L / 2], vi[C::L / 2];
-      if constexpr (C::L == 64) {
-        tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L), vr);
-        tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L + C::L), vi);
-        tmem_wait_ld();
-      } else {
-        uint32_t t0[32];
-        tmem_ld_16x256b_x8(abase + (uint32_t)(c * 2 * C::L), t0);
-        tmem_wait_ld();
+    for (int uu = 0; uu < 4; ++uu) {
+      const int u = u0 + uu;
+      float yr[2], yi[2];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) { vr[i] = t0[i]; vi[i] = t0[16 + i]; }
+      for (int o = 0; o < 2; ++o) {
+        const float RR = __uint_as_float(v[4 * uu + o]), IR = __uint_as_float(v[4 * uu + 2 + o]);
+        const float RI = __uint_as_float(v[16 + 4 * uu + o]), II = __uint_as_float(v[16 + 4 * uu + 2 + o]);
+        yr[o] = kInverse ? RR + II : RR - II;
+        yi[o] = kInverse ? RI - IR : IR + RI;
       }
-      // column-atom offsets of this signal's re / im planes
-      const uint32_t atom_re = (uint32_t)((c * 2 * C::L) / C::E) * C::LBO;
-      const uint32_t atom_im = (uint32_t)((c * 2 * C::L + C::L) / C::E) * C::LBO;
-      float* yre = nullptr;
-      float* yim = nullptr;
-      if constexpr (S == 3) {
-        const long long sig0 = tile * (2LL * C::TC) + 2 * c;
-        float* row = p.y + sig0 * C::N + C::L * ksv[bi] + 2 * l4;
-        if (sig0 < batch) yre = row;
-        if (sig0 + 1 < batch) yim = row + C::N;
-      }
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        float yr[2], yi[2];
+      const float4 k4 = cst[bi][u];
+      if constexpr (S == 0 || S == 2) {
+        // twiddle, then B(S+2)[K row = i0 + o][c, plane, ks]
 #pragma unroll
         for (int o = 0; o < 2; ++o) {
-          const float RR = __uint_as_float(vr[4 * u + o]), IR = __uint_as_float(vr[4 * u + 2 + o]);
-          const float RI = __uint_as_float(vi[4 * u + o]), II = __uint_as_float(vi[4 * u + 2 + o]);
-          yr[o] = kInverse ? RR + II : RR - II;
-          yi[o] = kInverse ? RI - IR : IR + RI;
+          const float wx = o ? k4.z : k4.x;
+          const float wy = kInverse ? -(o ? k4.w : k4.y) : (o ? k4.w : k4.y);
+          const float zr = yr[o] * wx - yi[o] * wy, zi = yr[o] * wy + yi[o] * wx;
+          const uint32_t off = 1024u * (uint32_t)u + ba[bi][o];
+          st_shared_b32(bdst + atom_re + off, __float_as_uint(round_tf32(zr)));
+          st_shared_b32(bdst + atom_im + off, __float_as_uint(round_tf32(zi)));
         }
-        const float4 k4 = cst[bi][u];
-        if constexpr (S == 0 || S == 2) {
-          // twiddle, then B(S+2)[K row = i0 + o][c, plane, ks]
-#pragma unroll
-          for (int o = 0; o < 2; ++o) {
-            const float wx = o ? k4.z : k4.x;
-            const float wy = kInverse ? -(o ? k4.w : k4.y) : (o ? k4.w : k4.y);
-            const float zr = yr[o] * wx - yi[o] * wy, zi = yr[o] * wy + yi[o] * wx;
-            const uint32_t off = 1024u * (uint32_t)u + ba[bi][o];
-            st_shared_b32(bdst + atom_re + off, __float_as_uint(round_tf32(zr)));
-            st_shared_b32(bdst + atom_im + off, __float_as_uint(round_tf32(zi)));
-          }
-        } else if constexpr (S == 1) {
-          // X[L ka + i0 + o] * H, written as the inverse's input B3[K row = ka][c, plane, i0 + o]
-          const float z0r = yr[0] * k4.x - yi[0] * k4.y, z0i = yr[0] * k4.y + yi[0] * k4.x;
-          const float z1r = yr[1] * k4.z - yi[1] * k4.w, z1i = yr[1] * k4.w + yi[1] * k4.z;
-          const uint32_t off = (uint32_t)(u / 4) * C::LBO + bb[bi][u % 4];
-          st_shared_v2(bdst + atom_re + off, round_tf32(z0r), round_tf32(z1r));
-          st_shared_v2(bdst + atom_im + off, round_tf32(z0i), round_tf32(z1i));
-        } else {
-          // outputs m = L ks + i0 + o: re -> signal 2c, im -> signal 2c+1
-          if (yre) *reinterpret_cast<float2*>(yre + 8 * u) = make_float2(yr[0], yr[1]);
-          if (yim) *reinterpret_cast<float2*>(yim + 8 * u) = make_float2(yi[0], yi[1]);
-        }
+      } else if constexpr (S == 1) {
+        // X[L ka + i0 + o] * H, written as the inverse's input B3[K row = ka][c, plane, i0 + o]
+        const float z0r = yr[0] * k4.x - yi[0] * k4.y, z0i = yr[0] * k4.y + yi[0] * k4.x;
+        const float z1r = yr[1] * k4.z - yi[1] * k4.w, z1i = yr[1] * k4.w + yi[1] * k4.z;
+        const uint32_t off = (uint32_t)(u / 4) * C::LBO + bb[bi][u % 4];
+        st_shared_v2(bdst + atom_re + off, round_tf32(z0r), round_tf32(z1r));
+        st_shared_v2(bdst + atom_im + off, round_tf32(z0i), round_tf32(z1i));
+      } else {
+        // outputs m = L ks + i0 + o: re -> signal 2c, im -> signal 2c+1
+        if (yre) *reinterpret_cast<float2*>(yre + 8 * u) = make_float2(yr[0], yr[1]);
+        if (yim) *reinterpret_cast<float2*>(yim + 8 * u) = make_float2(yi[0], yi[1]);
       }
+    }
+    if (pc < 3) {
+      tmem_wait_ld();
+      tmem_regs_ready(vbuf[(pc + 1) & 1]);
     }
   }
   tc_fence_before();

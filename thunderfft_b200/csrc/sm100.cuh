@@ -298,6 +298,15 @@ __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Registers written by an asynchronous tcgen05.ld are final only after
+// tcgen05.wait::ld; this empty asm (after the wait) makes every later use of
+// r depend on that point, so no use can be scheduled above the wait.
+template <int N>
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // 16 lanes x 256 bits, repeated 8 times (64 columns): thread t receives
 // r[4j+0..1] = (lane t/4, cols 8j+2(t%4)+{0,1}),
 // r[4j+2..3] = (lane t/4+8, same cols).
