@@ -241,6 +241,13 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
   using namespace sm100;
   using D = typename C::D;
+  // half2 C2C: the stage-2 tile is planar (re plane, im plane per signal), so a
+  // stage-2 epilogue thread holds two adjacent outputs and stores 8 bytes; a
+  // quad of lanes then writes 32 contiguous bytes (one full sector) per row.
+  // It costs the stage-1 epilogue a second (2-byte) shared store per output;
+  // measured on B200 it pays for N = 256, 1024, 2048 and not for 512, 4096.
+  constexpr bool kPlanar2 = C::kIsHalf && kEpi == kEpiNatural && kIn == kInNatural && C::NS % 8 == 0 &&
+                            (C::N == 256 || C::N == 1024 || C::N == 2048);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN];
@@ -483,9 +490,19 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
             const int sig = g1 * C::C1 + c1;
             const int g2 = sig / C::C2, c2 = sig % C::C2;
             const uint32_t krow = g2 * C::NA + a;
-            const int col = c2 * 2 * C::NS + 2 * ks;
-            const uint32_t off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
-            detail::store_complex<C::kIsHalf>(yb + off, yr * w.x - yi * w.y, yr * w.y + yi * w.x);
+            const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
+            if constexpr (kPlanar2) {
+              // planar stage-2 columns: re plane [c2*2NS, c2*2NS + NS), im plane after it
+              const int cre = c2 * 2 * C::NS + ks, cim = cre + C::NS;
+              const uint32_t ore = (cre / C::E) * C::LBO2 + D::swz(krow * 128u + (cre % C::E) * C::ESZ);
+              const uint32_t oim = (cim / C::E) * C::LBO2 + D::swz(krow * 128u + (cim % C::E) * C::ESZ);
+              st_shared_b16(yb + ore, __half_as_ushort(__float2half_rn(zr)));
+              st_shared_b16(yb + oim, __half_as_ushort(__float2half_rn(zi)));
+            } else {
+              const int col = c2 * 2 * C::NS + 2 * ks;
+              const uint32_t off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
+              detail::store_complex<C::kIsHalf>(yb + off, zr, zi);
+            }
           }
         }
       }
@@ -532,6 +549,44 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
         const uint32_t cols = 256u + ((C::M2 == 64) ? 0u : (uint32_t)(buf * C::N2));
         const int rp = block * 8 + (int)(lane >> 2);
         const int g2 = rp / C::NA, ka = rp % C::NA;
+        if constexpr (kPlanar2) {
+          const bool out8 = (reinterpret_cast<uintptr_t>(p.out) & 7u) == 0;
+          // re sub-chunk jr holds ks = 8 (jr mod d) + 2l + e of its signal; the
+          // im plane of the same outputs is d = NS/8 sub-chunks later
+          constexpr int d = C::NS / 8;
+          constexpr int GC2 = (2 * C::NS > 64) ? 2 : 1;   // chunks per signal plane pair
+          static_assert(CH % GC2 == 0, "planar stage-2 chunk groups");
+#pragma unroll
+          for (int c = 0; c < CH; c += GC2) {
+            uint32_t r[GC2][32];
+#pragma unroll
+            for (int g = 0; g < GC2; ++g) tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c + g) * 64, r[g]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int g = 0; g < GC2; ++g) tmem_regs_ready(r[g]);
+#pragma unroll
+            for (int qq = 0; qq < 4 * GC2; ++qq) {
+              const int jr = (qq / d) * 2 * d + (qq % d);
+              const int col = 64 * (ch0 + c) + 8 * jr + 2 * (int)(lane & 3u);
+              const int sl = g2 * C::C2 + col / (2 * C::NS);
+              const int ks = col % (2 * C::NS);
+              uint32_t hv[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int iRR = 4 * jr + e, iIR = 4 * jr + 2 + e, iRI = 4 * (jr + d) + e, iII = 4 * (jr + d) + 2 + e;
+                const float rr = __uint_as_float(r[iRR >> 5][iRR & 31]), ir = __uint_as_float(r[iIR >> 5][iIR & 31]);
+                const float ri = __uint_as_float(r[iRI >> 5][iRI & 31]), ii = __uint_as_float(r[iII >> 5][iII & 31]);
+                __half2 hh = __floats2half2_rn(rr - ii, ir + ri);
+                hv[e] = *reinterpret_cast<uint32_t*>(&hh);
+              }
+              if (sig0 + sl < batch) {
+                uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + (sig0 + sl) * C::N + C::NS * ka + ks;
+                if (out8) *reinterpret_cast<uint2*>(dst) = make_uint2(hv[0], hv[1]);
+                else { dst[0] = hv[0]; dst[1] = hv[1]; }   // output only 4-byte aligned
+              }
+            }
+          }
+        } else {
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
           uint32_t r[32];
@@ -563,6 +618,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
               }
             }
           }
+        }
         }
       }
       tc_fence_before();
