@@ -85,7 +85,7 @@ thff_status thff_selftest_wait_timeout(int limit_us, void* stream);
 /* ---- fused real 1-D FFT convolution --------------------------------------
  * Counterpart of the reference's fused conv1d sample
  * (sample/conv1d/conv1d_fullfft_l4096_thunder.cu:280-331), here for float
- * storage with TF32 tensor-core arithmetic.  For each of `batch` real
+ * storage.  For each of `batch` real
  * signals x[b] of length `lin` (zero-padded to n) and one real filter h:
  *     y[b][m] = (1/n) * sum_k x[b][(m-k) mod n] * h[k],   m < n,
  * computed as FFT -> multiply by the filter spectrum -> inverse FFT in ONE
@@ -108,6 +108,18 @@ thff_status thff_conv1d_async(int dtype, int n, int lin, const void* d_x, const 
 /* Same, then synchronizes `stream` and reports device-side errors. */
 thff_status thff_conv1d(int dtype, int n, int lin, const void* d_x, const void* d_spectrum, void* d_y,
                         long long batch, void* stream);
+
+/* Tensor-core arithmetic of the conv1d kernels (process-wide; default
+ * THFF_CONV_MIXED).  Stage 1 always reads the fp32 input as TF32.
+ *   THFF_CONV_MIXED: stages 2-4 take FP16 operands (the same 11-bit
+ *     significand as TF32) with FP32 accumulation; every FP16 operand is
+ *     scaled by an exact power of two chosen from a bound on its magnitude
+ *     (per tile for the stage-2 input, per call from max|H| for stage 3), so
+ *     any finite fp32 input stays in FP16 range.
+ *   THFF_CONV_TF32: all four stages TF32.
+ * No reference counterpart (the reference's conv1d is FP16 only). */
+enum { THFF_CONV_MIXED = 0, THFF_CONV_TF32 = 1 };
+thff_status thff_conv1d_set_arithmetic(int mode);
 
 /* ---- 2-D FFT convolution --------------------------------------------------
  * Counterpart of the reference's 2-D FFT convolution sample

@@ -10,6 +10,16 @@ import oracle
 GATE = 5e-3
 
 
+@pytest.fixture(params=["mixed", "tf32"])
+def arith(request):
+    """Both tensor-core arithmetics of the conv kernels; restores the default."""
+    import thunderfft_b200 as tf
+
+    tf.conv1d_set_arithmetic(request.param)
+    yield request.param
+    tf.conv1d_set_arithmetic("mixed")
+
+
 def run_conv(torch, tf, x, h, n):
     dx = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
     dh = torch.from_numpy(np.ascontiguousarray(h, dtype=np.float32)).cuda()
@@ -27,7 +37,7 @@ def padded(x, n):
 @pytest.mark.parametrize("n,lin,taps", [(4096, 3072, 1025), (4096, 4096, 9), (4096, 64, 53),
                                         (1024, 768, 257), (1024, 1024, 3), (1024, 32, 17)])
 @pytest.mark.parametrize("batch", [1, 2, 3, 7, 64])
-def test_conv1d_matches_direct_circular_convolution(cuda, n, lin, taps, batch):
+def test_conv1d_matches_direct_circular_convolution(cuda, arith, n, lin, taps, batch):
     import torch
 
     import thunderfft_b200 as tf
@@ -40,6 +50,29 @@ def test_conv1d_matches_direct_circular_convolution(cuda, n, lin, taps, batch):
     assert np.isfinite(y).all()
     e = oracle.rel_l2(y, ref)
     assert e <= GATE, (n, lin, taps, batch, e)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("xscale,hscale", [(1e6, 1.0), (1e-6, 1.0), (1.0, 1e5), (1.0, 1e-7), (3e7, 3e7), (1e-9, 1e-9)])
+def test_conv1d_range_scaling(cuda, arith, xscale, hscale):
+    """Inputs and filters far outside FP16's range: the mixed arithmetic scales
+    each FP16 operand by an exact power of two, so the relative error stays
+    that of N(0,1) data.  A tile of one huge sample among small ones is covered
+    too (per-tile scale from the tile's maximum)."""
+    import torch
+
+    import thunderfft_b200 as tf
+
+    n, lin, taps, batch = 4096, 3072, 1025, 6
+    rng = np.random.default_rng(17)
+    x = rng.standard_normal((batch, lin)) * xscale
+    x[3, 100] = 1e3 * xscale          # one spike: the tile's scale follows it
+    h = rng.standard_normal(taps) * hscale
+    y = run_conv(torch, tf, x.astype(np.float32), h.astype(np.float32), n)
+    ref = oracle.circconv1d(padded(x.astype(np.float32).astype(np.float64), n), h.astype(np.float32).astype(np.float64))
+    assert np.isfinite(y).all()
+    e = oracle.rel_l2(y, ref)
+    assert e <= GATE, (xscale, hscale, e)
 
 
 @pytest.mark.gpu
@@ -58,7 +91,7 @@ def test_conv1d_filter_spectrum_matches_fft(cuda):
 
 
 @pytest.mark.gpu
-def test_config4_full_size(cuda):
+def test_config4_full_size(cuda, arith):
     """16384 fp32 N(0,1) signals of length 3072, one
     1025-tap N(0,1) filter, padded to 4096 (circular = linear here)."""
     import torch
@@ -91,3 +124,6 @@ def test_conv1d_argument_contract():
     assert lib.thff_conv1d_async(0, 4096, 3072, 1 << 20, 1 << 20, 1 << 21, -1, None) == tf.THFF_INVALID_ARGUMENT
     assert lib.thff_conv1d_async(1, 4096, 3072, 1 << 20, 1 << 20, 1 << 21, 4, None) == tf.THFF_INVALID_ARGUMENT
     assert lib.thff_conv1d_async(0, 4096, 3072, 0, 0, 0, 0, None) == tf.THFF_OK
+    assert lib.thff_conv1d_set_arithmetic(7) == tf.THFF_INVALID_ARGUMENT
+    with pytest.raises(ValueError):
+        tf.conv1d_set_arithmetic(7)

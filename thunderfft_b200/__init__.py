@@ -34,7 +34,7 @@ __all__ = [
     "ThunderFFTInitialize", "ThunderFFTFinalize", "ThunderFFT_global", "c2c_async", "sync_check",
     "twiddle_table", "fft", "load_library", "library_path", "SUPPORTED_N", "batch_per_block",
     "warp_per_block", "threads_per_warp", "version", "conv1d_filter_spectrum", "conv1d",
-    "conv2d_filter_spectra", "conv2d", "conv2d_workspace",
+    "conv2d_filter_spectra", "conv2d", "conv2d_workspace", "conv1d_set_arithmetic",
 ]
 
 SUPPORTED_N = (64, 128, 256, 512, 1024, 2048, 4096)
@@ -90,6 +90,8 @@ def load_library() -> ctypes.CDLL:
     lib.thff_conv2d.restype = i32
     lib.thff_selftest_wait_timeout.argtypes = [i32, vp]
     lib.thff_selftest_wait_timeout.restype = i32
+    lib.thff_conv1d_set_arithmetic.argtypes = [i32]
+    lib.thff_conv1d_set_arithmetic.restype = i32
     for name in ("thff_initialize", "thff_finalize", "thff_twiddle_table", "thff_global",
                  "thff_c2c_async", "thff_sync_check", "thff_conv1d_filter_spectrum", "thff_conv1d_async",
                  "thff_conv1d"):
@@ -242,6 +244,17 @@ def conv1d(x, spectrum, n: int, out=None, stream=None, sync: bool = True):
     _check(fn(0, int(n), int(lin), x.data_ptr(), spectrum.data_ptr(), out.data_ptr(), int(batch),
               _stream_handle(st)))
     return out
+
+
+CONV_MIXED, CONV_TF32 = 0, 1
+
+
+def conv1d_set_arithmetic(mode) -> None:
+    """Tensor-core arithmetic of the conv1d kernels (process-wide):
+    "mixed" (default: TF32 first stage, FP16 operands with exact power-of-two
+    range scaling for stages 2-4, FP32 accumulation) or "tf32"."""
+    code = {"mixed": CONV_MIXED, "tf32": CONV_TF32}.get(mode, mode)
+    _check(load_library().thff_conv1d_set_arithmetic(int(code)))
 
 
 def conv2d_workspace(h: int, w: int, pairs: int, device=None):

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -411,10 +412,10 @@ thff_status dispatch_c2c(DeviceState& st, const Consts& c, int dtype, int n, con
   return fail(THFF_INVALID_ARGUMENT, "[ThunderFFT] unsupported FFT length");
 }
 
-template <int kN>
+template <int kN, bool kMixed>
 thff_status launch_conv1d(DeviceState& st, const Consts& c, int lin, const void* x, const void* spec, void* y,
                           long long batch, cudaStream_t stream) {
-  using C = thff::Conv1dCfg<kN>;
+  using C = thff::Conv1dCfg<kN, kMixed>;
   CUtensorMap map;
   std::memset(&map, 0, sizeof(map));
   const uint64_t dims[4] = {uint64_t(C::E), uint64_t(lin / C::L), uint64_t(C::H), uint64_t(batch)};
@@ -424,9 +425,11 @@ thff_status launch_conv1d(DeviceState& st, const Consts& c, int lin, const void*
                          CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
   if (s != THFF_OK) return s;
   thff::Conv1dParams p;
+  std::memset(&p, 0, sizeof(p));
   p.x = static_cast<const float*>(x);
   p.y = static_cast<float*>(y);
   p.a = c.a1;
+  p.a16 = c.a2;
   p.tw = reinterpret_cast<const float2*>(c.tw);
   p.spec = static_cast<const float2*>(spec);
   p.batch = batch;
@@ -442,6 +445,10 @@ thff_status launch_conv1d(DeviceState& st, const Consts& c, int lin, const void*
   return THFF_OK;
 }
 
+// Arithmetic of the conv1d stages 2-4: THFF_CONV_MIXED (FP16 operands with
+// per-tile power-of-two range scaling) or THFF_CONV_TF32.
+std::atomic<int> g_conv1d_arith{THFF_CONV_MIXED};
+
 // Stage matrix + twiddles of the conv kernel: the forward DFT matrix of
 // length L = sqrt(n) (one group) and the forward twiddles of length n.
 thff_status get_conv_consts(DeviceState& st, int n, const Consts** out) {
@@ -452,6 +459,7 @@ thff_status get_conv_consts(DeviceState& st, int n, const Consts** out) {
     const int L = n == 4096 ? 64 : 32;
     thff_status s = upload(build_stage_matrix(L, 1, -1, false), &c.a1);
     if (s != THFF_OK) return s;
+    if ((s = upload(build_stage_matrix(L, 1, -1, true), &c.a2)) != THFF_OK) return s;   // FP16 image
     std::vector<uint8_t> tw(size_t(n) * 8);
     for (int k = 0; k < n; ++k) {
       const double th = -kTau * double(k) / double(n);
@@ -767,8 +775,18 @@ thff_status thff_conv1d_async(int dtype, int n, int lin, const void* d_x, const 
     if ((s = get_conv_consts(*st, n, &c)) != THFF_OK) return s;
   }
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  return n == 4096 ? launch_conv1d<4096>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs)
-                   : launch_conv1d<1024>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs);
+  if (g_conv1d_arith.load() == THFF_CONV_MIXED)
+    return n == 4096 ? launch_conv1d<4096, true>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs)
+                     : launch_conv1d<1024, true>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs);
+  return n == 4096 ? launch_conv1d<4096, false>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs)
+                   : launch_conv1d<1024, false>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs);
+}
+
+thff_status thff_conv1d_set_arithmetic(int mode) {
+  if (mode != THFF_CONV_MIXED && mode != THFF_CONV_TF32)
+    return fail(THFF_INVALID_ARGUMENT, "conv1d: arithmetic must be THFF_CONV_MIXED or THFF_CONV_TF32");
+  g_conv1d_arith.store(mode);
+  return THFF_OK;
 }
 
 thff_status thff_conv1d(int dtype, int n, int lin, const void* d_x, const void* d_spectrum, void* d_y,
