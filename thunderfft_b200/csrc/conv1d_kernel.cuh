@@ -422,28 +422,32 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(&bar_const, 0, p.err, kDevTimeoutMma);
-      const uint32_t a = smem_u32(smem + C::OFF_A), a16 = smem_u32(smem + C::OFF_A16);
       const uint32_t idesc = instr_desc(D::kFmt, C::M, C::NCOL, 0, 1);
       const uint32_t idesc16 = instr_desc(kFmtF16, C::M, C::NCOL, 0, 1);
       const uint32_t lboA = (C::M / 8) * 128;
       const int ks1 = (p.rows_valid + 7) / 8;  // stage 1 skips all-zero K rows
-      auto stage_tf32 = [&](uint32_t d, uint32_t b, int ksteps) {
-#pragma unroll 1
-        for (int k = 0; k < ksteps; ++k) {
-          const uint64_t ad = smem_desc(a + k * 2 * lboA, lboA, 128, kSwNone);
-          const uint64_t bd = smem_desc(b + k * 1024u, C::LBO, D::kBSbo, D::kBSwizzle);
-          umma_tf32(d, ad, bd, idesc, k > 0);
-        }
+      // All descriptors are built once; a K step adds its byte offset >> 4 to
+      // the start-address field (addresses < 256 KB never carry out of it).
+      // The K loops are fully unrolled: a single issuing thread that rebuilds
+      // descriptors per MMA cannot keep the tensor core fed.
+      const uint64_t adA = smem_desc(smem_u32(smem + C::OFF_A), lboA, 128, kSwNone);
+      const uint64_t adA16 = smem_desc(smem_u32(smem + C::OFF_A16), lboA, 128, kSwNone);
+      // input slot i / B tile i: the descriptor of slot 0 / B2 plus i tiles
+      const uint64_t bdIn0 = smem_desc(smem_u32(smem + C::OFF_IN), C::LBO, D::kBSbo, D::kBSwizzle);
+      const uint64_t bdB0 = C::kF16 ? smem_desc(smem_u32(bbuf), C::LBO, 1024, kSw128)
+                                    : smem_desc(smem_u32(bbuf), C::LBO, D::kBSbo, D::kBSwizzle);
+      // TF32: K step of 8 = 2 A core columns, 8 B rows (1024 B)
+      auto stage_tf32 = [&](uint32_t d, uint64_t bd, int ksteps) {
+#pragma unroll
+        for (int k = 0; k < C::KSTEPS; ++k)
+          if (k < ksteps)
+            umma_tf32(d, adA + (uint64_t)((k * 2 * lboA) >> 4), bd + (uint64_t)((k * 1024) >> 4), idesc, k > 0);
       };
-      // FP16 operands: A K-major no swizzle (16 elements = 32 B per K step),
-      // B MN-major 128-B swizzle (16 K rows = 2048 B per K step)
-      auto stage_f16 = [&](uint32_t d, uint32_t b) {
-#pragma unroll 1
-        for (int k = 0; k < C::KSTEPS16; ++k) {
-          const uint64_t ad = smem_desc(a16 + k * 2 * lboA, lboA, 128, kSwNone);
-          const uint64_t bd = smem_desc(b + k * 2048u, C::LBO, 1024, kSw128);
-          umma_f16(d, ad, bd, idesc16, k > 0);
-        }
+      // FP16: K step of 16 = 2 A core columns, 16 B rows (2048 B)
+      auto stage_f16 = [&](uint32_t d, uint64_t bd) {
+#pragma unroll
+        for (int k = 0; k < C::KSTEPS16; ++k)
+          umma_f16(d, adA16 + (uint64_t)((k * 2 * lboA) >> 4), bd + (uint64_t)((k * 2048) >> 4), idesc16, k > 0);
       };
       for (int r = 0; ok && r < T + 3; ++r) {
         // S1(r): input slot -> D0
@@ -452,7 +456,7 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
           if (!mbar_wait(&bar_in_full[slot], (uint32_t)(r / C::SIN) & 1u, p.err, kDevTimeoutMma) ||
               !mbar_wait(&bar_d_empty[0], ((uint32_t)r & 1u) ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
-          stage_tf32(detail::acc_addr<C>(tmem, 0, 0, 0), smem_u32(smem + C::OFF_IN + slot * C::TILE_BYTES), ks1);
+          stage_tf32(detail::acc_addr<C>(tmem, 0, 0, 0), bdIn0 + (uint64_t)(slot * (C::TILE_BYTES >> 4)), ks1);
           umma_commit(&bar_in_empty[slot]);
           umma_commit(&bar_d_full[0]);
         }
@@ -464,9 +468,9 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
           if (!mbar_wait(&bar_b_full[s - 1], (uint32_t)j & 1u, p.err, kDevTimeoutMma) ||
               !mbar_wait(&bar_d_empty[s], ((uint32_t)j & 1u) ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t bsrc = smem_u32(bbuf + (s - 1) * C::BT_BYTES);
-          if constexpr (C::kF16) stage_f16(detail::acc_addr<C>(tmem, s, 0, 0), bsrc);
-          else stage_tf32(detail::acc_addr<C>(tmem, s, 0, 0), bsrc, C::KSTEPS);
+          const uint64_t bd = bdB0 + (uint64_t)((s - 1) * (C::BT_BYTES >> 4));
+          if constexpr (C::kF16) stage_f16(detail::acc_addr<C>(tmem, s, 0, 0), bd);
+          else stage_tf32(detail::acc_addr<C>(tmem, s, 0, 0), bd, C::KSTEPS);
           umma_commit(&bar_b_empty[s - 1]);
           umma_commit(&bar_d_full[s]);
         }
