@@ -354,18 +354,25 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
       // A images: K-major, no swizzle, core matrix (8 rows x 16 B) contiguous;
       // LBO = K-direction core stride = M/8 * 128 B, SBO = 128 B.
       const uint32_t lboA1 = (C::M1 / 8) * 128, lboA2 = (C::M2 / 8) * 128;
+      // Descriptors are built once; a K step, an input slot or a Y buffer adds
+      // its byte offset >> 4 to the start-address field (shared addresses
+      // < 256 KB never carry out of it).  The issuing thread then spends a
+      // few integer adds per MMA.
+      const uint64_t adA1 = smem_desc(a1, lboA1, 128, kSwNone), adA2 = smem_desc(a2, lboA2, 128, kSwNone);
+      const uint64_t bdIn0 = smem_desc(smem_u32(smem + C::OFF_IN), C::LBO1, D::kBSbo, D::kBSwizzle);
+      const uint64_t bdY0 = smem_desc(smem_u32(smem + C::OFF_Y), C::LBO2, D::kBSbo, D::kBSwizzle);
       for (int i = 0; ok && i <= my_tiles; ++i) {
         if (i < my_tiles) {
           const int slot = i % C::SIN, buf = i & 1;
           if (!mbar_wait(&bar_in_full[slot], (uint32_t)(i / C::SIN) & 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
           if (!mbar_wait(&bar_acc1_empty[buf], ((uint32_t)(i >> 1) & 1u) ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t b = smem_u32(smem + C::OFF_IN + slot * C::TILE_BYTES);
+          const uint64_t bd0 = bdIn0 + (uint64_t)(slot * (C::TILE_BYTES >> 4));
           const uint32_t d = (C::M1 == 64) ? tmem + ((uint32_t)(16 * buf) << 16) : tmem + (uint32_t)(buf * C::N1);
 #pragma unroll
           for (int k = 0; k < C::KSTEPS1; ++k) {
-            const uint64_t ad = smem_desc(a1 + k * 2 * lboA1, lboA1, 128, kSwNone);
-            const uint64_t bd = smem_desc(b + k * C::KSTEP_BYTES, C::LBO1, D::kBSbo, D::kBSwizzle);
+            const uint64_t ad = adA1 + (uint64_t)((k * 2 * lboA1) >> 4);
+            const uint64_t bd = bd0 + (uint64_t)((k * C::KSTEP_BYTES) >> 4);
             if constexpr (C::kIsHalf) umma_f16(d, ad, bd, idesc1, k > 0);
             else umma_tf32(d, ad, bd, idesc1, k > 0);
           }
@@ -378,13 +385,13 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
           if (!mbar_wait(&bar_y_full[buf], ph, p.err, kDevTimeoutMma)) { ok = false; break; }
           if (!mbar_wait(&bar_acc2_empty[buf], ph ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t b = smem_u32(smem + C::OFF_Y + buf * C::TILE_BYTES);
+          const uint64_t bd0 = bdY0 + (uint64_t)(buf * (C::TILE_BYTES >> 4));
           const uint32_t d = (C::M2 == 64) ? tmem + 256u + ((uint32_t)(16 * buf) << 16)
                                            : tmem + 256u + (uint32_t)(buf * C::N2);
 #pragma unroll
           for (int k = 0; k < C::KSTEPS2; ++k) {
-            const uint64_t ad = smem_desc(a2 + k * 2 * lboA2, lboA2, 128, kSwNone);
-            const uint64_t bd = smem_desc(b + k * C::KSTEP_BYTES, C::LBO2, D::kBSbo, D::kBSwizzle);
+            const uint64_t ad = adA2 + (uint64_t)((k * 2 * lboA2) >> 4);
+            const uint64_t bd = bd0 + (uint64_t)((k * C::KSTEP_BYTES) >> 4);
             if constexpr (C::kIsHalf) umma_f16(d, ad, bd, idesc2, k > 0);
             else umma_tf32(d, ad, bd, idesc2, k > 0);
           }
