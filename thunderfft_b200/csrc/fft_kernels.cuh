@@ -107,12 +107,16 @@ template <> struct Fft2Shape<false, 128, 1> { static constexpr int NS = 4,  NA =
 template <> struct Fft2Shape<false, 256, 1> { static constexpr int NS = 8,  NA = 32, G1 = 4, G2 = 1, T = 16, SIN = 4, EPW = 2; };
 template <> struct Fft2Shape<false, 512, 1> { static constexpr int NS = 16, NA = 32, G1 = 2, G2 = 1, T = 8,  SIN = 4, EPW = 2; };
 
-template <bool kHalf, int kN, int kVar = 0>
+template <bool kHalf, int kN, int kVar = 0, int kHSlots = 0>
 struct Fft2Cfg {
   using D = DType<kHalf>;
   using S = Fft2Shape<kHalf, kN, kVar>;
   static constexpr bool kIsHalf = kHalf;
-  static constexpr int N = kN, NS = S::NS, NA = S::NA, G1 = S::G1, G2 = S::G2, T = S::T, SIN = S::SIN;
+  // kHSlots > 0 (kEpiMulNatural): the producer stages each tile's spectrum
+  // rows in shared memory (kHSlots slots); the input ring shrinks to 2 tiles.
+  static constexpr int HS = kHSlots;
+  static constexpr int N = kN, NS = S::NS, NA = S::NA, G1 = S::G1, G2 = S::G2, T = S::T;
+  static constexpr int SIN = (kHSlots > 0 && S::SIN > 2) ? 2 : S::SIN;
   static_assert(NS * NA == N, "factorization");
   static constexpr int ESZ = D::kEsz, E = D::kElemsPer128B;
   static constexpr int C1 = T / G1, C2 = T / G2;          // signals along MMA N per stage
@@ -138,7 +142,8 @@ struct Fft2Cfg {
   static constexpr uint32_t OFF_A2 = (A1_BYTES + 1023) / 1024 * 1024;
   static constexpr uint32_t OFF_IN = OFF_A2 + (A2_BYTES + 1023) / 1024 * 1024;
   static constexpr uint32_t OFF_Y = OFF_IN + SIN * TILE_BYTES;
-  static constexpr uint32_t SMEM_DATA = OFF_Y + 2 * TILE_BYTES;
+  static constexpr uint32_t OFF_H = OFF_Y + 2 * TILE_BYTES;   // spectrum tiles (kHSlots)
+  static constexpr uint32_t SMEM_DATA = OFF_H + HS * TILE_BYTES;
   static constexpr uint32_t SMEM_BYTES = exclusive_smem(SMEM_DATA + 1024 /*align slack*/);
   static_assert(SMEM_BYTES + 512 <= 232448, "shared memory budget");
   static constexpr int EPW = S::EPW;                       // epilogue warps per TMEM lane quadrant
@@ -238,7 +243,8 @@ __device__ __forceinline__ uint32_t in_tile_offset(int sig, int s, int a) {
 // ---------------------------------------------------------------------------
 template <class C, int kEpi = kEpiNatural, int kIn = kInNatural>
 __global__ void __launch_bounds__(C::kThreads, 1)
-fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
+fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__ CUtensorMap tmap_spec,
+            const FftParams p) {
   using namespace sm100;
   using D = typename C::D;
   // half2 C2C: the stage-2 tile is planar (re plane, im plane per signal), so a
@@ -253,7 +259,9 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
   __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN];
   __shared__ uint64_t bar_acc1_full[2], bar_acc1_empty[2], bar_y_full[2], bar_y_empty[2];
   __shared__ uint64_t bar_acc2_full[2], bar_acc2_empty[2], bar_const, bar_done;
+  __shared__ uint64_t bar_h_full[C::HS > 0 ? C::HS : 1], bar_h_empty[C::HS > 0 ? C::HS : 1];
   __shared__ uint32_t tmem_slot;
+  constexpr bool kStageH = kEpi == kEpiMulNatural && C::HS > 0;   // spectrum tiles via TMA
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const long long batch = p.batch;
@@ -271,6 +279,8 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
     }
     mbar_init(&bar_const, 1);
     mbar_init(&bar_done, 1);
+    if constexpr (kStageH)
+      for (int i = 0; i < C::HS; ++i) { mbar_init(&bar_h_full[i], 1); mbar_init(&bar_h_empty[i], C::kEpiWarps); }
     fence_mbar_init();
   }
   if (warp == 1) { tmem_alloc(&tmem_slot, 512); tmem_relinquish(); }
@@ -283,6 +293,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       if (p.use_tma) tma_prefetch_desc(&tmap_in);
+      if constexpr (kStageH) tma_prefetch_desc(&tmap_spec);
       // constant stage matrices (bulk copies of host-built images)
       mbar_arrive_expect_tx(&bar_const, C::A1_BYTES + C::A2_BYTES);
       bulk_load(smem + C::OFF_A1, p.a1, C::A1_BYTES, &bar_const);
@@ -342,6 +353,23 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_in_full[slot]);
+      }
+      if constexpr (kStageH) {
+        // spectrum rows of this tile: spec[ch][r0 .. r0+T)[0 .. N) = T*N complex,
+        // one 2-D box of 128-B lines (128-B swizzle against bank conflicts).
+        // Issued after the tile's input: the slot frees when the previous
+        // tile's stage-2 epilogue ends, which needs this tile's stage 1.
+        const int hs = i % C::HS;
+        if (!mbar_wait_warp(&bar_h_empty[hs], ((uint32_t)(i / C::HS) & 1u) ^ 1u, p.err, kDevTimeoutProducer)) break;
+        if (lane == 0) {
+          const long long sig0 = tile * C::T;
+          const long long img = sig0 / p.rows, r0 = sig0 - img * p.rows;
+          const long long pg = p.pair0 + img, ch = pg / p.ppc;
+          mbar_arrive_expect_tx(&bar_h_full[hs], C::TILE_BYTES);
+          tma_load_3d(smem + C::OFF_H + hs * C::TILE_BYTES, &tmap_spec, &bar_h_full[hs], 0,
+                      (int)(((ch * p.rows + r0) * C::N) / 16), 0);
+        }
+        __syncwarp();
       }
     }
   } else if (warp == 1) {
@@ -531,7 +559,11 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
       const int buf = i & 1;
       const uint32_t ph = (uint32_t)(i >> 1) & 1u;
       if (!mbar_wait_warp(&bar_acc2_full[buf], ph, p.err, kDevTimeoutEpilogue)) break;
+      const int hs = kStageH ? i % (C::HS > 0 ? C::HS : 1) : 0;
+      if constexpr (kStageH)
+        if (!mbar_wait_warp(&bar_h_full[hs], (uint32_t)(i / C::HS) & 1u, p.err, kDevTimeoutEpilogue)) break;
       tc_fence_after();
+      const uint32_t hbase = smem_u32(smem + C::OFF_H + hs * C::TILE_BYTES);
       const long long sig0 = tile * C::T;
       // conv2d modes: all T signals of a tile lie in one image (R % T == 0,
       // checked by the host), so the image bookkeeping is per tile.
@@ -612,7 +644,14 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
               if constexpr (kEpi == kEpiNatural) {
                 detail::store_out<C::kIsHalf>(p.out, (sig0 + sl) * C::N + k, xr, xi);
               } else if constexpr (kEpi == kEpiMulNatural) {
-                const float2 w = __ldg(spec_t + sl * C::N + k);
+                float2 w;
+                if constexpr (kStageH) {
+                  // 128-B-swizzled staging: 16-B chunk XOR (128-B line % 8)
+                  const uint32_t byte = (uint32_t)(sl * C::N + k) * 8u;
+                  w = ld_shared_v2f(hbase + (byte ^ (((byte >> 7) & 7u) << 4)));
+                } else {
+                  w = __ldg(spec_t + sl * C::N + k);
+                }
                 detail::store_out<C::kIsHalf>(p.out, (sig0 + sl) * C::N + k, xr * w.x - xi * w.y, xr * w.y + xi * w.x);
               } else if constexpr (kEpi == kEpiBlocked) {
                 const int lb = p.blk_log2;
@@ -630,7 +669,10 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const FftParams p) {
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_acc2_empty[buf]);
+      if (lane == 0) {
+        mbar_arrive(&bar_acc2_empty[buf]);
+        if constexpr (kStageH) mbar_arrive(&bar_h_empty[hs]);
+      }
     }
   }
 

@@ -370,6 +370,11 @@ __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ void st_shared_v2(uint32_t saddr, float a, float b) {
   asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(saddr), "f"(a), "f"(b) : "memory");
 }
+__device__ __forceinline__ float2 ld_shared_v2f(uint32_t saddr) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(saddr) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_shared_b16(uint32_t saddr, unsigned short v) {
   asm volatile("st.shared.b16 [%0], %1;" ::"r"(saddr), "h"(v) : "memory");
 }

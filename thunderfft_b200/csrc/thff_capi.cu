@@ -318,10 +318,11 @@ thff_status encode_conv_input(CUtensorMap* map, const void* in, const thff::FftP
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, in, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
-template <bool kHalf, int kN, int kEpi = thff::kEpiNatural, int kIn = thff::kInNatural, int kVar = 0>
+template <bool kHalf, int kN, int kEpi = thff::kEpiNatural, int kIn = thff::kInNatural, int kVar = 0,
+          int kHS = 0>
 thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* out, long long batch,
                         cudaStream_t stream, const thff::FftParams* extra = nullptr) {
-  using C = thff::Fft2Cfg<kHalf, kN, kVar>;
+  using C = thff::Fft2Cfg<kHalf, kN, kVar, kHS>;
   const long long num_tiles = (batch + C::T - 1) / C::T;
   const long long full_tiles = batch / C::T;
   const bool use_tma = kIn != thff::kInNatural || aligned16(in);
@@ -360,11 +361,26 @@ thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* 
   p.in = in; p.out = out; p.a1 = c.a1; p.a2 = c.a2; p.tw = reinterpret_cast<const float2*>(c.tw);
   p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = st.d_err;
   if (!extra) { p.rows = 1; p.chans = 1; p.ppc = 1; }
+  // spectrum staging (kEpiMulNatural with slots): the spectra as 128-B lines,
+  // one box = the T*N complex values of one tile
+  CUtensorMap map_spec;
+  std::memset(&map_spec, 0, sizeof(map_spec));
+  if constexpr (kEpi == thff::kEpiMulNatural && kHS > 0) {
+    static_assert(!kHalf && (C::T * C::N) % 16 == 0 && C::T * C::N / 16 <= 256, "spectrum box");
+    const uint64_t lines = uint64_t(p.chans) * uint64_t(p.rows) * C::N / 16;
+    const uint64_t dims[3] = {32, lines, 1};
+    const uint64_t strides[2] = {128, lines * 128};
+    const uint32_t box[3] = {32, uint32_t(C::T * C::N / 16), 1};
+    if (!p.spec || !aligned16(p.spec)) return fail(THFF_INVALID_ARGUMENT, "[ThunderFFT] conv2d pass: spectrum");
+    thff_status s = encode(&map_spec, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, p.spec, dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != THFF_OK) return s;
+  }
   auto kernel = thff::fft2_kernel<C, kEpi, kIn>;
   thff_status s = set_smem_attr(st, kernel, int(C::SMEM_BYTES));
   if (s != THFF_OK) return s;
   const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
-  kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map, p);
+  kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map, map_spec, p);
   THFF_CUDA(cudaGetLastError(), "ThunderFFT_global launch");
   return THFF_OK;
 }
@@ -488,18 +504,29 @@ int conv2d_c1(int n) {
 
 // One pass of the 2-D convolution pipeline: length-n C2C transform of
 // `batch` signals with input mode kIn and stage-2 epilogue mode kEpi.
+// Spectrum staging slots of the length-n multiply pass: two when they fit
+// beside a 2-tile input ring, else one (computed without instantiating the
+// configuration that would not fit).
+template <int kN>
+constexpr int conv2d_hslots() {
+  using B = thff::Fft2Cfg<false, kN>;
+  return (B::OFF_IN + (2 + 2 + 2) * B::TILE_BYTES + 1024 + 512 <= 232448u) ? 2 : 1;
+}
+
 template <int kEpi, int kIn>
 thff_status conv2d_pass(DeviceState& st, const Consts& c, int n, const void* in, void* out, long long batch,
                         const thff::FftParams& extra, cudaStream_t cs) {
-  // the pair-planar pass uses the NA = 32 shape variant where one exists
+  // the pair-planar pass uses the NA = 32 shape variant where one exists;
+  // the spectrum-multiply pass stages the spectrum tiles in shared memory
   constexpr int kV = (kIn == thff::kInPairPlanar) ? 1 : 0;
+  constexpr bool kMul = kEpi == thff::kEpiMulNatural;
   switch (n) {
-    case 128: return launch_fft2<false, 128, kEpi, kIn, kV>(st, c, in, out, batch, cs, &extra);
-    case 256: return launch_fft2<false, 256, kEpi, kIn, kV>(st, c, in, out, batch, cs, &extra);
-    case 512: return launch_fft2<false, 512, kEpi, kIn, kV>(st, c, in, out, batch, cs, &extra);
-    case 1024: return launch_fft2<false, 1024, kEpi, kIn>(st, c, in, out, batch, cs, &extra);
-    case 2048: return launch_fft2<false, 2048, kEpi, kIn>(st, c, in, out, batch, cs, &extra);
-    case 4096: return launch_fft2<false, 4096, kEpi, kIn>(st, c, in, out, batch, cs, &extra);
+    case 128: return launch_fft2<false, 128, kEpi, kIn, kV, kMul ? conv2d_hslots<128>() : 0>(st, c, in, out, batch, cs, &extra);
+    case 256: return launch_fft2<false, 256, kEpi, kIn, kV, kMul ? conv2d_hslots<256>() : 0>(st, c, in, out, batch, cs, &extra);
+    case 512: return launch_fft2<false, 512, kEpi, kIn, kV, kMul ? conv2d_hslots<512>() : 0>(st, c, in, out, batch, cs, &extra);
+    case 1024: return launch_fft2<false, 1024, kEpi, kIn, 0, kMul ? conv2d_hslots<1024>() : 0>(st, c, in, out, batch, cs, &extra);
+    case 2048: return launch_fft2<false, 2048, kEpi, kIn, 0, kMul ? conv2d_hslots<2048>() : 0>(st, c, in, out, batch, cs, &extra);
+    case 4096: return launch_fft2<false, 4096, kEpi, kIn, 0, kMul ? conv2d_hslots<4096>() : 0>(st, c, in, out, batch, cs, &extra);
   }
   return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
 }
