@@ -121,6 +121,34 @@ thff_status thff_conv1d(int dtype, int n, int lin, const void* d_x, const void* 
 enum { THFF_CONV_MIXED = 0, THFF_CONV_TF32 = 1 };
 thff_status thff_conv1d_set_arithmetic(int mode);
 
+/* ---- tiled (overlap-save) 1-D convolution ---------------------------------
+ * Counterpart of the reference's tiled conv1d sample (sample/conv1d/main.cu:
+ * 38-129, 214-276): each of `batch` complex sequences x[b] (input_len
+ * elements, float2 for THFF_F32 or half2 for THFF_F16) is cut into 64-point
+ * windows advancing by V = 65 - f; every window goes through FFT -> x filter
+ * spectrum -> inverse FFT and keeps its first V outputs.  Result: the valid
+ * correlation with the complex filter g (f <= 64 taps),
+ *     y[b][i] = sum_{k<f} x[b][i + k] g[k],   i < input_len - f + 1,
+ * stored as y[b][input_len - f + 1] in the input's storage type.  The
+ * window chain is applied as one precomputed operator (see
+ * thff_conv1d_tiled_operator) by the N = 64 tensor-core kernel. */
+
+/* Bytes of the operator buffer for `dtype`. */
+long long thff_conv1d_tiled_operator_bytes(int dtype);
+
+/* Builds the operator of filter g (f complex fp32 taps on the device, f in
+ * [1, 64]) for `dtype` in d_operator (16-byte aligned, size above).  The
+ * reference prepares the filter spectrum with cuFFT (main.cu:145-153,
+ * 253-265). */
+thff_status thff_conv1d_tiled_operator(int dtype, const void* d_filter, int f, void* d_operator, void* stream);
+
+/* Asynchronous tiled convolution; thff_conv1d_tiled also synchronizes
+ * `stream` and reports device-side errors. */
+thff_status thff_conv1d_tiled_async(int dtype, long long input_len, int f, const void* d_x, const void* d_operator,
+                                    void* d_y, long long batch, void* stream);
+thff_status thff_conv1d_tiled(int dtype, long long input_len, int f, const void* d_x, const void* d_operator,
+                              void* d_y, long long batch, void* stream);
+
 /* ---- 2-D FFT convolution --------------------------------------------------
  * Counterpart of the reference's 2-D FFT convolution sample
  * (sample/conv2d/thunder.cu:70-207,410-592: row FFT, column FFT x H x

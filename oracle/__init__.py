@@ -118,6 +118,16 @@ def circconv1d(x: np.ndarray, h: np.ndarray, threads: int = 0) -> np.ndarray:
     return y
 
 
+def corr1d_valid(x: np.ndarray, g: np.ndarray) -> np.ndarray:
+    """Valid complex correlation y[b][i] = sum_{k<f} x[b][i + k] g[k],
+    i < L - f + 1, in FP64 — the check of the reference's tiled conv1d sample
+    (sample/conv1d/main.cu:157-172, reference_conv1d_valid)."""
+    x = np.atleast_2d(np.asarray(x, dtype=np.complex128))
+    g = np.asarray(g, dtype=np.complex128)
+    # numpy.correlate(a, v)[k] = sum_n a[n + k] conj(v[n])
+    return np.stack([np.correlate(row, np.conj(g), mode="valid") for row in x])
+
+
 def circconv2d(x: np.ndarray, filters: np.ndarray, filt_index: np.ndarray, threads: int = 0) -> np.ndarray:
     """y[b] = x[b] (*) filters[filt_index[b]] (2-D circular, FP64)."""
     x = np.ascontiguousarray(x, dtype=np.float64)

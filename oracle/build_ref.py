@@ -1,9 +1,16 @@
-"""Build recipe for oracle/_ref/libthff_ref.so — TEST INFRASTRUCTURE ONLY.
+"""Build recipe for oracle/_ref/ — TEST INFRASTRUCTURE ONLY.
 
-Compiles oracle/ref_harness.cu against the reference's own headers where they
-lie (/root/reference/include, read-only) for sm_100a with nvcc directly (the
-reference's CMake build is not used).  Output goes only to oracle/_ref/.
-Run in the build container:  python oracle/build_ref.py
+Compiles, for sm_100a with nvcc directly (the reference's CMake build is not
+used), from the reference sources where they lie (/root/reference, read-only):
+  libthff_ref.so        oracle/ref_harness.cu against the reference headers
+                        (its ThunderFFT_global, for parity and GPU timing);
+  ref_conv1d_tiled      the reference's tiled conv1d sample as it is
+                        (sample/conv1d/main.cu);
+  ref_conv1d_full       the reference's fused FFT-conv sample as it is
+                        (sample/conv1d/conv1d_fullfft_l4096_thunder.cu).
+The two samples link cuFFT (they prepare their filter spectra with it).
+Output goes only to oracle/_ref/.  Run in the build container:
+    python oracle/build_ref.py
 """
 from __future__ import annotations
 
@@ -16,21 +23,42 @@ REF_INCLUDE = Path("/root/reference/include")
 OUT = HERE / "_ref" / "libthff_ref.so"
 
 
+REF = Path("/root/reference")
+SAMPLES = {
+    "ref_conv1d_tiled": REF / "sample" / "conv1d" / "main.cu",
+    "ref_conv1d_full": REF / "sample" / "conv1d" / "conv1d_fullfft_l4096_thunder.cu",
+}
+NVCC = "/usr/local/cuda/bin/nvcc"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def build_sample(name: str, src: Path) -> None:
+    out = HERE / "_ref" / name
+    if out.exists() and out.stat().st_mtime >= src.stat().st_mtime:
+        return
+    tmp = out.with_suffix(".tmp")
+    subprocess.run([NVCC, "-std=c++17", "-O3", *ARCH, "-I", str(REF_INCLUDE), str(src), "-lcufft", "-o", str(tmp)],
+                   check=True)
+    tmp.replace(out)
+    print(out)
+
+
 def main() -> int:
     if not REF_INCLUDE.exists():
         print("reference sources not present; nothing to build")
         return 0
     src = HERE / "ref_harness.cu"
-    if OUT.exists() and OUT.stat().st_mtime >= src.stat().st_mtime:
-        return 0
     OUT.parent.mkdir(exist_ok=True)
-    tmp = OUT.with_suffix(".so.tmp")
-    cmd = ["/usr/local/cuda/bin/nvcc", "-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a",
-           "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-cudart", "static", "-I", str(REF_INCLUDE),
-           str(src), "-o", str(tmp)]
-    subprocess.run(cmd, check=True)
-    tmp.replace(OUT)
-    print(OUT)
+    if not (OUT.exists() and OUT.stat().st_mtime >= src.stat().st_mtime):
+        tmp = OUT.with_suffix(".so.tmp")
+        cmd = [NVCC, "-std=c++17", "-O3", *ARCH, "-shared", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+               "-cudart", "static", "-I", str(REF_INCLUDE), str(src), "-o", str(tmp)]
+        subprocess.run(cmd, check=True)
+        tmp.replace(OUT)
+        print(OUT)
+    for name, sample in SAMPLES.items():
+        if sample.exists():
+            build_sample(name, sample)
     return 0
 
 

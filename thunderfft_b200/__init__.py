@@ -35,6 +35,7 @@ __all__ = [
     "twiddle_table", "fft", "load_library", "library_path", "SUPPORTED_N", "batch_per_block",
     "warp_per_block", "threads_per_warp", "version", "conv1d_filter_spectrum", "conv1d",
     "conv2d_filter_spectra", "conv2d", "conv2d_workspace", "conv1d_set_arithmetic",
+    "conv1d_tiled_operator", "conv1d_tiled",
 ]
 
 SUPPORTED_N = (64, 128, 256, 512, 1024, 2048, 4096)
@@ -92,6 +93,14 @@ def load_library() -> ctypes.CDLL:
     lib.thff_selftest_wait_timeout.restype = i32
     lib.thff_conv1d_set_arithmetic.argtypes = [i32]
     lib.thff_conv1d_set_arithmetic.restype = i32
+    lib.thff_conv1d_tiled_operator_bytes.argtypes = [i32]
+    lib.thff_conv1d_tiled_operator_bytes.restype = i64
+    lib.thff_conv1d_tiled_operator.argtypes = [i32, vp, i32, vp, vp]
+    lib.thff_conv1d_tiled_operator.restype = i32
+    lib.thff_conv1d_tiled_async.argtypes = [i32, i64, i32, vp, vp, vp, i64, vp]
+    lib.thff_conv1d_tiled_async.restype = i32
+    lib.thff_conv1d_tiled.argtypes = [i32, i64, i32, vp, vp, vp, i64, vp]
+    lib.thff_conv1d_tiled.restype = i32
     for name in ("thff_initialize", "thff_finalize", "thff_twiddle_table", "thff_global",
                  "thff_c2c_async", "thff_sync_check", "thff_conv1d_filter_spectrum", "thff_conv1d_async",
                  "thff_conv1d"):
@@ -247,6 +256,50 @@ def conv1d(x, spectrum, n: int, out=None, stream=None, sync: bool = True):
 
 
 CONV_MIXED, CONV_TF32 = 0, 1
+
+
+def conv1d_tiled_operator(filt, T="float", stream=None):
+    """Operator of the tiled (overlap-save) convolution for the complex filter
+    taps `filt` (complex64 CUDA tensor, 1 <= len <= 64), for storage type T
+    (reference: the padded filter's cuFFT spectrum, sample/conv1d/main.cu:145-153)."""
+    import torch
+
+    if not (filt.is_cuda and filt.dtype == torch.complex64 and filt.dim() == 1 and filt.is_contiguous()):
+        raise ValueError("filter must be a contiguous 1-D complex64 CUDA tensor")
+    code = _dtype_code(T)
+    lib = load_library()
+    op = torch.empty(int(lib.thff_conv1d_tiled_operator_bytes(code)), dtype=torch.uint8, device=filt.device)
+    st = stream if stream is not None else torch.cuda.current_stream(filt.device)
+    _check(lib.thff_conv1d_tiled_operator(code, filt.data_ptr(), int(filt.numel()), op.data_ptr(),
+                                          _stream_handle(st)))
+    op.filter_length = int(filt.numel())
+    return op
+
+
+def conv1d_tiled(x, operator, f: Optional[int] = None, out=None, stream=None, sync: bool = True):
+    """Tiled 64-point FFT convolution of every row of x (valid correlation
+    with the operator's filter): x complex64 [batch, L] (float2 / TF32) or
+    float16 [batch, L, 2] (half2 / FP16); returns [batch, L - f + 1] of the
+    same type (reference: sample/conv1d/main.cu:38-129)."""
+    import torch
+
+    f = int(f if f is not None else getattr(operator, "filter_length"))
+    if x.dtype == torch.complex64:
+        T, L, shape = "float", x.shape[-1], lambda b, n: (b, n)
+    elif x.dtype == torch.float16 and x.shape[-1] == 2:
+        T, L, shape = "half", x.shape[-2], lambda b, n: (b, n, 2)
+    else:
+        raise ValueError("x must be complex64 [batch, L] or float16 [batch, L, 2]")
+    if not (x.is_cuda and x.is_contiguous()):
+        raise ValueError("x must be a contiguous CUDA tensor")
+    batch = x.numel() // (L * (1 if T == "float" else 2))
+    if out is None:
+        out = torch.empty(shape(batch, L - f + 1), dtype=x.dtype, device=x.device)
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    fn = load_library().thff_conv1d_tiled if sync else load_library().thff_conv1d_tiled_async
+    _check(fn(_dtype_code(T), int(L), f, x.data_ptr(), operator.data_ptr(), out.data_ptr(), int(batch),
+              _stream_handle(st)))
+    return out
 
 
 def conv1d_set_arithmetic(mode) -> None:

@@ -173,6 +173,15 @@ struct FftParams {
   long long nimg_b;      // B (images per channel)
   long long ppc;         // image pairs per channel = ceil(B / 2)
   int blk_log2;          // kEpiBlocked: log2 of the block width Cb
+  // Overlapping windows (dft1_kernel<C, true>, the tiled convolution): signal
+  // w is window t = w % win_per_sig of sequence b = w / win_per_sig, i.e.
+  // in[b][t*win_stride + n] (zero past in_len); only its first win_stride
+  // outputs are stored, at out[b][t*win_stride + n] (n < out_len - t*win_stride).
+  int win_stride;
+  long long win_per_sig;
+  long long in_len;
+  long long out_len;
+  long long win_tmax;    // last window index lying wholly inside its sequence (-1: none)
 };
 
 // Stage-2 epilogue output modes.
@@ -708,7 +717,7 @@ struct Dft1Cfg {
   static constexpr int kThreads = 192;                   // producer, MMA, 4 epilogue warps
 };
 
-template <class C>
+template <class C, bool kWin = false>
 __global__ void __launch_bounds__(C::kThreads, 1)
 dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__ CUtensorMap tmap_out,
             const FftParams p, int use_tma_store) {
@@ -744,6 +753,15 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
   auto tile_off = [](int sig, int col) -> uint32_t {
     return (uint32_t)(col / C::E) * (C::T * 128u) + sw128((uint32_t)sig * 128u + (col % C::E) * C::ESZ);
   };
+  // Window mode: a tile whose 128 windows lie in one sequence and wholly
+  // inside it moves by one TMA box in and one bulk copy out (when the host
+  // found the strides 16-byte aligned); other tiles take thread loads/stores.
+  auto interior = [&](long long tile, long long& b0, long long& t0) -> bool {
+    const long long w0 = tile * C::T;
+    b0 = w0 / p.win_per_sig;
+    t0 = w0 - b0 * p.win_per_sig;
+    return t0 + C::T <= p.win_per_sig && t0 + C::T - 1 <= p.win_tmax;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -756,12 +774,47 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
       const int slot = i % C::SIN;
       if (!mbar_wait_warp(&bar_in_empty[slot], ((uint32_t)(i / C::SIN) & 1u) ^ 1u, p.err, kDevTimeoutProducer)) break;
       uint8_t* dst = smem + C::OFF_IN + slot * C::TILE_BYTES;
-      if (p.use_tma) {
+      long long wb0 = 0, wt0 = 0;
+      if (!kWin && p.use_tma) {
         if (lane == 0) {
           mbar_arrive_expect_tx(&bar_in_full[slot], C::TILE_BYTES);
           tma_load_3d(dst, &tmap_in, &bar_in_full[slot], 0, (int)(tile * C::T), 0);
         }
         __syncwarp();
+      } else if (kWin && p.use_tma && interior(tile, wb0, wt0)) {
+        // 128 windows = rows of a 4-D map {element, window (stride V), atom, sequence}
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bar_in_full[slot], C::TILE_BYTES);
+          tma_load_4d(dst, &tmap_in, &bar_in_full[slot], 0, (int)wt0, 0, (int)wb0);
+        }
+        __syncwarp();
+      } else if constexpr (kWin) {
+        // overlapping windows by thread loads, zero past each sequence's end;
+        // each window's 64 elements are contiguous (two per lane)
+        const long long w0 = tile * C::T;
+        const uint32_t base = smem_u32(dst);
+        long long b = w0 / p.win_per_sig, t = w0 - b * p.win_per_sig;
+        for (int sig = 0; sig < C::T; ++sig) {
+          const bool live = w0 + sig < batch;
+#pragma unroll
+          for (int h = 0; h < C::N / 32; ++h) {
+            const int n = (int)lane + 32 * h;
+            const long long e = t * p.win_stride + n;
+            const bool ok = live && e < p.in_len;
+            const long long gi = b * p.in_len + e;
+            const uint32_t off = tile_off(sig, 2 * n);
+            if constexpr (C::kIsHalf) {
+              st_shared_b32(base + off, ok ? __ldg(reinterpret_cast<const unsigned int*>(p.in) + gi) : 0u);
+            } else {
+              const float2 v = ok ? __ldg(reinterpret_cast<const float2*>(p.in) + gi) : make_float2(0.f, 0.f);
+              st_shared_v2(base + off, v.x, v.y);
+            }
+          }
+          if (++t == p.win_per_sig) { t = 0; ++b; }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_in_full[slot]);
       } else {
         const long long sig0 = tile * C::T;
         const uint32_t base = smem_u32(dst);
@@ -828,12 +881,29 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
       const uint32_t sbase = smem_u32(stage);
       const int sig = (int)(32 * q + lane);
       const long long gsig = tile * C::T + sig;
+      long long wb0 = 0, wt0 = 0;
+      const bool win_bulk = kWin && use_tma_store && interior(tile, wb0, wt0);
 #pragma unroll 1
       for (int chunk = 0; chunk < 4; ++chunk) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + ((32u * q) << 16) + (uint32_t)(buf * 128 + chunk * 32), r);
         tmem_wait_ld();
-        if (use_tma_store) {
+        if (win_bulk) {
+          // window sig's first V outputs, contiguous after window sig-1's
+#pragma unroll
+          for (int u = 0; u < 16; ++u) {
+            const int j = chunk * 16 + u;
+            if (j < p.win_stride) {
+              const uint32_t o = (uint32_t)(sig * p.win_stride + j) * (uint32_t)(2 * C::ESZ);
+              if constexpr (C::kIsHalf) {
+                __half2 t2 = __floats2half2_rn(__uint_as_float(r[2 * u]), __uint_as_float(r[2 * u + 1]));
+                st_shared_b32(sbase + o, *reinterpret_cast<uint32_t*>(&t2));
+              } else {
+                st_shared_v2(sbase + o, __uint_as_float(r[2 * u]), __uint_as_float(r[2 * u + 1]));
+              }
+            }
+          }
+        } else if (!kWin && use_tma_store) {
           if constexpr (C::kIsHalf) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
@@ -851,10 +921,22 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
               st_shared_v4(sbase + tile_off(sig, chunk * 32 + 4 * v), r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
           }
         } else if (gsig < batch) {
+          if constexpr (kWin) {
+            // the window's first win_stride outputs that lie inside its sequence
+            const long long b = gsig / p.win_per_sig, t = gsig - b * p.win_per_sig;
+            const long long o0 = t * p.win_stride, rem = p.out_len - o0;
+            const int lim = (int)(rem < p.win_stride ? rem : p.win_stride);
 #pragma unroll
-          for (int u = 0; u < 16; ++u)
-            detail::store_out<C::kIsHalf>(p.out, gsig * C::N + chunk * 16 + u, __uint_as_float(r[2 * u]),
-                                          __uint_as_float(r[2 * u + 1]));
+            for (int u = 0; u < 16; ++u)
+              if (chunk * 16 + u < lim)
+                detail::store_out<C::kIsHalf>(p.out, b * p.out_len + o0 + chunk * 16 + u, __uint_as_float(r[2 * u]),
+                                              __uint_as_float(r[2 * u + 1]));
+          } else {
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+              detail::store_out<C::kIsHalf>(p.out, gsig * C::N + chunk * 16 + u, __uint_as_float(r[2 * u]),
+                                            __uint_as_float(r[2 * u + 1]));
+          }
         }
       }
       // Hand-off: each epilogue warp arrives on staged[buf] after its part of
@@ -870,7 +952,14 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
         if (lane == 0) ok = mbar_wait(&bar_staged[buf], (uint32_t)(i >> 1) & 1u, p.err, kDevTimeoutEpilogue);
         if (!__shfl_sync(0xffffffffu, (int)ok, 0)) break;
         if (lane == 0) {
-          if (use_tma_store) {
+          if (win_bulk) {
+            // the tile's outputs: one contiguous span of 128 V elements
+            uint8_t* g = reinterpret_cast<uint8_t*>(p.out) +
+                         (wb0 * p.out_len + wt0 * p.win_stride) * (long long)(2 * C::ESZ);
+            bulk_store(g, stage, (uint32_t)(C::T * p.win_stride * 2 * C::ESZ));
+            bulk_commit_group();
+            bulk_wait_group_read<1>();
+          } else if (!kWin && use_tma_store) {
             tma_store_3d(&tmap_out, stage, 0, (int)(tile * C::T), 0);
             bulk_commit_group();
             bulk_wait_group_read<1>();   // the previous tile's store has read its slot
@@ -882,7 +971,7 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
       __syncwarp();
     }
     if (warp == 2 && lane == 0) {
-      if (use_tma_store) bulk_wait_group<0>();
+      if (use_tma_store) bulk_wait_group<0>();   // (window mode: bulk stores)
       if (pending_slot >= 0) mbar_arrive(&bar_in_empty[pending_slot]);
     }
   }

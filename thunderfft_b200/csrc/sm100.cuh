@@ -181,6 +181,14 @@ __device__ __forceinline__ void tma_store_4d(const void* tmap, const void* smem_
       : "memory");
 }
 
+// Plain (non-tensor) bulk copy shared -> global, tracked by bulk async-groups;
+// both addresses 16-byte aligned, size % 16 == 0.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

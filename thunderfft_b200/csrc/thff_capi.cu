@@ -24,6 +24,7 @@
 #include "fft_kernels.cuh"
 #include "conv1d_kernel.cuh"
 #include "conv2d_kernels.cuh"
+#include "conv1d_tiled.cuh"
 
 namespace {
 
@@ -410,6 +411,47 @@ thff_status launch_dft1(DeviceState& st, const Consts& c, const void* in, void* 
   const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
   kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map_in, map_out, p, tma_store ? 1 : 0);
   THFF_CUDA(cudaGetLastError(), "ThunderFFT_global launch");
+  return THFF_OK;
+}
+
+// Tiled (overlap-save) convolution: the N = 64 kernel in window mode with
+// the filter's circulant operator as its B matrix.
+template <bool kHalf>
+thff_status launch_conv1d_tiled(DeviceState& st, const void* op, const void* in, void* out, long long nseq,
+                                long long in_len, int f, cudaStream_t stream) {
+  using C = thff::Dft1Cfg<kHalf>;
+  const long long out_len = in_len - f + 1, stride = C::N - f + 1;
+  const long long wps = (out_len + stride - 1) / stride;   // windows per sequence
+  const long long windows = wps * nseq;
+  const long long num_tiles = (windows + C::T - 1) / C::T;
+  CUtensorMap map_in, map_out;
+  std::memset(&map_in, 0, sizeof(map_in));
+  std::memset(&map_out, 0, sizeof(map_out));
+  thff::FftParams p;
+  std::memset(&p, 0, sizeof(p));
+  const uint64_t csz = 2 * C::ESZ;   // bytes per complex element
+  // Fast tiles (128 windows inside one sequence): a TMA box in when the
+  // window stride and the sequence stride are 16-byte multiples, one bulk copy
+  // of the contiguous outputs out when the output side is aligned as well.
+  const bool tma_in = aligned16(in) && (stride * csz) % 16 == 0 && (in_len * csz) % 16 == 0;
+  const bool bulk_out = aligned16(out) && (stride * csz) % 16 == 0 && (nseq == 1 || (out_len * csz) % 16 == 0);
+  thff_status s;
+  if (tma_in) {
+    const uint64_t dims[4] = {uint64_t(C::E), uint64_t(wps), uint64_t(C::KATOMS), uint64_t(nseq)};
+    const uint64_t strides[3] = {uint64_t(stride) * csz, 128, uint64_t(in_len) * csz};
+    const uint32_t box[4] = {uint32_t(C::E), uint32_t(C::T), uint32_t(C::KATOMS), 1};
+    if ((s = encode(&map_in, kHalf ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, in, dims,
+                    strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) != THFF_OK)
+      return s;
+  }
+  p.in = in; p.out = out; p.a1 = op; p.batch = windows; p.use_tma = tma_in ? 1 : 0; p.err = st.d_err;
+  p.win_stride = int(stride); p.win_per_sig = wps; p.in_len = in_len; p.out_len = out_len;
+  p.win_tmax = in_len >= C::N ? (in_len - C::N) / stride : -1;
+  auto kernel = thff::dft1_kernel<C, true>;
+  if ((s = set_smem_attr(st, kernel, int(C::SMEM_BYTES))) != THFF_OK) return s;
+  const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
+  kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map_in, map_out, p, bulk_out ? 1 : 0);
+  THFF_CUDA(cudaGetLastError(), "tiled conv1d launch");
   return THFF_OK;
 }
 
@@ -807,6 +849,68 @@ thff_status thff_conv1d_async(int dtype, int n, int lin, const void* d_x, const 
                      : launch_conv1d<1024, true>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs);
   return n == 4096 ? launch_conv1d<4096, false>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs)
                    : launch_conv1d<1024, false>(*st, *c, lin, d_x, d_spectrum, d_y, batch, cs);
+}
+
+long long thff_conv1d_tiled_operator_bytes(int dtype) {
+  if (!valid_dtype(dtype)) return -1;
+  return 128LL * 128LL * (dtype == THFF_F16 ? 2 : 4);
+}
+
+thff_status thff_conv1d_tiled_operator(int dtype, const void* d_filter, int f, void* d_operator, void* stream) {
+  if (!valid_dtype(dtype)) return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: dtype must be THFF_F32 or THFF_F16");
+  if (f < 1 || f > 64) return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: filter length must be in [1, 64]");
+  if (!d_filter || !d_operator) return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: null pointer");
+  if (!aligned16(d_operator) || (reinterpret_cast<uintptr_t>(d_filter) & 7u))
+    return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: operator must be 16-byte aligned, filter 8-byte aligned");
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    DeviceState* st;
+    if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
+  }
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  const int total = 128 * 128;
+  if (dtype == THFF_F16)
+    thff::conv1d_tiled_operator_kernel<true><<<(total + 255) / 256, 256, 0, cs>>>(
+        static_cast<const float2*>(d_filter), f, static_cast<uint8_t*>(d_operator));
+  else
+    thff::conv1d_tiled_operator_kernel<false><<<(total + 255) / 256, 256, 0, cs>>>(
+        static_cast<const float2*>(d_filter), f, static_cast<uint8_t*>(d_operator));
+  THFF_CUDA(cudaGetLastError(), "tiled conv1d operator launch");
+  return THFF_OK;
+}
+
+thff_status thff_conv1d_tiled_async(int dtype, long long input_len, int f, const void* d_x, const void* d_operator,
+                                    void* d_y, long long batch, void* stream) {
+  if (!valid_dtype(dtype)) return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: dtype must be THFF_F32 or THFF_F16");
+  if (f < 1 || f > 64) return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: filter length must be in [1, 64]");
+  if (input_len < f) return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: input length must be >= filter length");
+  if (batch < 0) return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: batch must be nonnegative");
+  if (batch == 0) return THFF_OK;
+  if (!d_x || !d_operator || !d_y) return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: null pointer");
+  const uintptr_t esz = dtype == THFF_F16 ? 4 : 8;
+  if ((reinterpret_cast<uintptr_t>(d_x) % esz) || (reinterpret_cast<uintptr_t>(d_y) % esz) || !aligned16(d_operator))
+    return fail(THFF_INVALID_ARGUMENT, "tiled conv1d: x/y must be element aligned, the operator 16-byte aligned");
+  int dev;
+  thff_status s = current_device(&dev);
+  if (s != THFF_OK) return s;
+  DeviceState* st;
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
+  }
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  return dtype == THFF_F16 ? launch_conv1d_tiled<true>(*st, d_operator, d_x, d_y, batch, input_len, f, cs)
+                           : launch_conv1d_tiled<false>(*st, d_operator, d_x, d_y, batch, input_len, f, cs);
+}
+
+thff_status thff_conv1d_tiled(int dtype, long long input_len, int f, const void* d_x, const void* d_operator,
+                              void* d_y, long long batch, void* stream) {
+  thff_status s = thff_conv1d_tiled_async(dtype, input_len, f, d_x, d_operator, d_y, batch, stream);
+  if (s != THFF_OK || batch == 0) return s;
+  return thff_sync_check(stream);
 }
 
 thff_status thff_conv1d_set_arithmetic(int mode) {
