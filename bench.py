@@ -397,31 +397,6 @@ def main():
     per_launch_us = ms / launches * 1e3
     achieved = BYTES_PER_TRANSFORM_BATCH / (per_launch_us / 1e6) / 1e9
 
-    # ---- the reference's own GPU code (recompiled for sm_100a) on the same
-    # buffers, through its public ThunderFFT_global (which synchronizes per call)
-    ref_gpu = None
-    if not args.no_extras and rank == 0:
-        try:
-            import oracle
-
-            if oracle.ref_available():
-                def ref_step():
-                    oracle.ref_global(DTYPE, N, True, x.data_ptr(), y.data_ptr(), BATCH, stream.cuda_stream)
-                    oracle.ref_global(DTYPE, N, False, y.data_ptr(), z.data_ptr(), BATCH, stream.cuda_stream)
-                ref_step()
-                r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                r0.record(stream)
-                for _ in range(5):
-                    ref_step()
-                r1.record(stream)
-                torch.cuda.synchronize(dev)
-                rms = r0.elapsed_time(r1) / 5
-                ref_gpu = {"value": 2 * BYTES_PER_TRANSFORM_BATCH / (rms / 1e3) / 1e9, "unit": "GB/s",
-                           "ms_per_step": rms,
-                           "what": "reference ThunderFFT_global (mma.sync) recompiled for sm_100a, same buffers, 1 GPU"}
-        except Exception as e:  # pragma: no cover
-            ref_gpu = {"error": str(e)}
-
     # ---- cuFFT on the same GPU / same buffers (extra comparison point)
     cufft = None
     if args.no_extras or DTYPE != "float":
@@ -509,7 +484,6 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks.summary(),
             "cufft": cufft,
-            "reference_gpu": ref_gpu,
             "roundtrip_rel_l2": rt_err,
         }
         print(json.dumps(line), flush=True)

@@ -191,6 +191,12 @@ def ref_available() -> bool:
     return REF_LIB.exists()
 
 
+def ref_sample(name: str) -> Path:
+    """Path of a reference sample binary built by oracle/build_ref.py
+    (ref_conv1d_tiled, ref_conv1d_full); may not exist."""
+    return HERE / "_ref" / name
+
+
 def ref_lib():
     global _ref
     if _ref is None:

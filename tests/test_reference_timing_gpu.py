@@ -1,0 +1,107 @@
+"""Side-by-side GPU timings against the reference's own code, recompiled for
+sm_100a from its sources (oracle/build_ref.py; skipped when oracle/_ref is
+absent).  Each test also checks that both sides ran; the timings print with
+`pytest -s` and are summarised under profiles/:
+
+    python -m pytest tests/test_reference_timing_gpu.py -m gpu -q -s
+
+  * C2C, BASELINE config 2 (N=1024 TF32, batch 65536): our thff_global vs the
+    reference's ThunderFFT_global on the same buffers (both synchronize).
+  * Tiled conv1d (sample/conv1d/main.cu): a 2^24-element half2 sequence,
+    9 taps, vs the sample binary (it times its kernel with CUDA events).
+  * Fused FFT convolution (sample/conv1d/conv1d_fullfft_l4096_thunder.cu):
+    the sample's FP16 kernel on 16384 x 4096 inputs, 1025 taps, filter FFT
+    excluded, vs our config-4 kernel (16384 fp32 signals of 3072 -> 4096).
+"""
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle
+
+
+def _ev(torch):
+    return torch.cuda.Event(enable_timing=True)
+
+
+def _time(torch, fn, reps):
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = _ev(torch), _ev(torch)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps * 1e3  # us
+
+
+def _run_sample(name, args, pattern):
+    exe = oracle.ref_sample(name)
+    if not exe.exists():
+        pytest.skip(f"{exe} not built")
+    out = subprocess.run([str(exe), *map(str, args)], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    m = re.search(pattern, out.stdout)
+    assert m, out.stdout[-2000:]
+    return float(m.group(1)) * 1e3  # ms -> us
+
+
+@pytest.mark.gpu
+def test_c2c_config2_vs_reference(cuda):
+    import torch
+
+    import thunderfft_b200 as tf
+
+    if not oracle.ref_available():
+        pytest.skip("reference library not built")
+    n, batch = 1024, 65536
+    x = torch.complex(torch.rand(batch, n, device="cuda") * 2 - 1, torch.rand(batch, n, device="cuda") * 2 - 1)
+    y = torch.empty_like(x)
+    st = torch.cuda.current_stream().cuda_stream
+    ours = _time(torch, lambda: tf.ThunderFFT_global("float", n, True, x, y, batch), 10)
+    ref = _time(torch, lambda: oracle.ref_global("float", n, True, x.data_ptr(), y.data_ptr(), batch, st), 5)
+    gb = 2 * n * batch * 8 / 1e9
+    print(f"\n| C2C config 2 (N=1024 TF32 fwd, batch 65536) | ours {ours:.1f} us ({gb / ours * 1e6:.0f} GB/s) "
+          f"| reference ThunderFFT_global {ref:.1f} us ({gb / ref * 1e6:.0f} GB/s) | ratio {ref / ours:.2f}x |")
+    assert ours > 0 and ref > 0
+
+
+@pytest.mark.gpu
+def test_tiled_conv1d_vs_reference_sample(cuda):
+    import torch
+
+    import thunderfft_b200 as tf
+
+    L, f = 1 << 24, 9
+    ref = _run_sample("ref_conv1d_tiled", [L, f, 0, 0, 5, 20], r"Kernel pipeline time:\s*([0-9.]+)\s*ms")
+    g = torch.randn(f, dtype=torch.complex64, device="cuda")
+    op = tf.conv1d_tiled_operator(g, "half")
+    x = torch.view_as_real(torch.randn(1, L, dtype=torch.complex64, device="cuda")).half().contiguous()
+    out = torch.empty(1, L - f + 1, 2, dtype=torch.float16, device="cuda")
+    ours = _time(torch, lambda: tf.conv1d_tiled(x, op, f, out=out, sync=False), 20)
+    mb = (2 * L - f + 1) * 4 / 1e6
+    print(f"\n| tiled conv1d half2, L=2^24, f=9 | ours {ours:.1f} us ({mb / ours * 1e3:.0f} GB/s) "
+          f"| reference sample kernel {ref:.1f} us ({mb / ref * 1e3:.0f} GB/s) | ratio {ref / ours:.2f}x |")
+    assert ours > 0 and ref > 0
+
+
+@pytest.mark.gpu
+def test_fused_conv1d_vs_reference_sample(cuda):
+    import torch
+
+    import thunderfft_b200 as tf
+
+    ref = _run_sample("ref_conv1d_full", [4096, 1025, 0, 16384, 1, 5, 30, 0, 0],
+                      r"time:\s*([0-9.]+)\s*ms")
+    batch, lin, taps, n = 16384, 3072, 1025, 4096
+    x = torch.randn(batch, lin, device="cuda")
+    spec = tf.conv1d_filter_spectrum(torch.randn(taps, device="cuda"), n)
+    y = torch.empty(batch, n, device="cuda")
+    ours = _time(torch, lambda: tf.conv1d(x, spec, n, out=y, sync=False), 20)
+    print(f"\n| fused conv1d, 16384 signals -> 4096 | ours (fp32 in/out, config 4) {ours:.1f} us "
+          f"| reference sample (fp16 in/out, 4096-sample inputs) {ref:.1f} us | ratio {ref / ours:.2f}x |")
+    assert ours > 0 and ref > 0
