@@ -7,8 +7,12 @@ used), from the reference sources where they lie (/root/reference, read-only):
   ref_conv1d_tiled      the reference's tiled conv1d sample as it is
                         (sample/conv1d/main.cu);
   ref_conv1d_full       the reference's fused FFT-conv sample as it is
-                        (sample/conv1d/conv1d_fullfft_l4096_thunder.cu).
-The two samples link cuFFT (they prepare their filter spectra with it).
+                        (sample/conv1d/conv1d_fullfft_l4096_thunder.cu);
+  ref_paper_fft         the reference's device-API timing CLI
+                        (sample/bench/paper_fft.cu, with its util/ and
+                        baseline/ include directories and --use_fast_math,
+                        as its CMakeLists builds it).
+The samples link cuFFT (they use it for filter spectra or accuracy checks).
 Output goes only to oracle/_ref/.  Run in the build container:
     python oracle/build_ref.py
 """
@@ -27,6 +31,11 @@ REF = Path("/root/reference")
 SAMPLES = {
     "ref_conv1d_tiled": REF / "sample" / "conv1d" / "main.cu",
     "ref_conv1d_full": REF / "sample" / "conv1d" / "conv1d_fullfft_l4096_thunder.cu",
+    "ref_paper_fft": REF / "sample" / "bench" / "paper_fft.cu",
+}
+EXTRA_FLAGS = {
+    "ref_paper_fft": ["-I", str(REF / "sample" / "bench" / "util"), "-I", str(REF / "sample" / "bench" / "baseline"),
+                      "--use_fast_math"],
 }
 NVCC = "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -37,8 +46,8 @@ def build_sample(name: str, src: Path) -> None:
     if out.exists() and out.stat().st_mtime >= src.stat().st_mtime:
         return
     tmp = out.with_suffix(".tmp")
-    subprocess.run([NVCC, "-std=c++17", "-O3", *ARCH, "-I", str(REF_INCLUDE), str(src), "-lcufft", "-o", str(tmp)],
-                   check=True)
+    subprocess.run([NVCC, "-std=c++17", "-O3", *ARCH, "-I", str(REF_INCLUDE), *EXTRA_FLAGS.get(name, []), str(src),
+                    "-lcufft", "-o", str(tmp)], check=True)
     tmp.replace(out)
     print(out)
 

@@ -51,6 +51,30 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+PAPER_FFT_SRC = PKG / "bench" / "paper_fft.cu"
+PAPER_FFT = PKG / "bench" / "thff_paper_fft"
+
+
+def build_paper_fft(force: bool = False) -> Path:
+    """The device-API timing CLI (bench/paper_fft.cu), linked like a C++ user
+    of the library links it (header + -lthunderfft_b200, plus cuFFT for its
+    accuracy check)."""
+    lib = build()
+    headers = list((ROOT / "include").rglob("*.h*"))
+    if (not force and PAPER_FFT.exists() and
+            all(p.stat().st_mtime <= PAPER_FFT.stat().st_mtime for p in [PAPER_FFT_SRC, lib, *headers])):
+        return PAPER_FFT
+    cmd = [nvcc(), *ARCH_FLAGS, "-std=c++17", "-O3", "-I", str(ROOT / "include"), str(PAPER_FFT_SRC), "-o",
+           str(PAPER_FFT), "-L", str(lib.parent), "-lthunderfft_b200", "-lcufft", "-Xlinker", f"-rpath={lib.parent}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("nvcc failed building thff_paper_fft")
+    return PAPER_FFT
+
+
 if __name__ == "__main__":
     build(force="--force" in sys.argv, verbose="-v" in sys.argv)
     print(LIB)
+    if "--paper-fft" in sys.argv:
+        print(build_paper_fft(force="--force" in sys.argv))
