@@ -4,14 +4,29 @@
 // The reference's device routine (ThunderFFT_kernel_reg, shared_kernel_n*.cuh)
 // is a warp-MMA register FFT with size-specific fragment maps.  This library
 // keeps its calling contract (block shape, 32-element fragments, caller
-// workspace and barriers) but computes it as a self-sorting (Stockham)
-// radix-4 FFT over the caller's shared-memory workspace, FP32 arithmetic
-// with exactly reduced twiddles (sincospif), FP16 storage rounding between
-// passes for half.  Fused kernels keep their data on chip; the large batched
-// transforms use the tcgen05 kernels behind ThunderFFT_global.
+// workspace and barriers) and computes it as a mixed-radix self-sorting
+// (Stockham) FFT in FP32 registers:
+//
+//   * thread t of the P = 32 * warp_per_block<N> threads holds elements
+//     n = t + P*m (m < M = N/P) of each of its signals, so the first pass is
+//     an M-point DFT over the thread's own fragment and needs no exchange;
+//   * the middle passes (radix 2..16) run butterflies q = t + P*h, read and
+//     written through the caller's workspace with a per-exchange padding
+//     that keeps the shared-memory accesses free of bank conflicts;
+//   * the last pass is again M-point with butterfly j = t, so its outputs
+//     k = t + P*r land in the fragment convention with no exchange.
+//
+// Radix plans (first | middle | last): 64: 2|16|2, 128: 4|8|4,
+// 256: 2|8|8|2, 512: 16|2|16, 1024: 32|32, 2048: 32|2|32, 4096: 32|4|32.
+// Register DFTs are radix-2 decimation in frequency with compile-time roots;
+// inter-pass twiddles come from a few exact sincospif anchors (every 8th
+// power) and short power chains.  half data is widened to FP32 on entry,
+// rounded to half2 in the workspace exchanges and on exit.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+
+#include <utility>
 
 #include "util_arith.h"
 #include "util_cuda.h"
@@ -30,75 +45,214 @@ __device__ __forceinline__ vec2_t<T> from_f2(float2 v) {
   else return v;
 }
 
-// exp(sign * 2*pi*i * num / den) with exact argument reduction.
-__device__ __forceinline__ float2 unit_root(int num, int den, bool forward) {
+namespace dfft {
+
+// ---- compile-time roots of unity ------------------------------------------
+struct CRoot {
+  double c, s;
+};
+
+// (cos, sin)(2*pi*k/n): exact quadrant reduction in integers, then a Taylor
+// series on [0, pi/2) in double.
+__host__ __device__ constexpr CRoot croot(int k, int n) {
+  k %= n;
+  if (k < 0) k += n;
+  const int q = (4 * k) / n;
+  const int rem = 4 * k - q * n;  // angle inside the quadrant = (pi/2) * rem / n
+  const double x = 1.5707963267948966192 * double(rem) / double(n);
+  double s = x, c = 1.0, ts = x, tc = 1.0;
+  for (int i = 1; i < 16; ++i) {
+    ts *= -x * x / double((2 * i) * (2 * i + 1));
+    tc *= -x * x / double((2 * i - 1) * (2 * i));
+    s += ts;
+    c += tc;
+  }
+  if (rem == 0) {
+    s = 0.0;
+    c = 1.0;
+  }
+  switch (q) {
+    case 1: return CRoot{-s, c};
+    case 2: return CRoot{-c, -s};
+    case 3: return CRoot{s, -c};
+    default: return CRoot{c, s};
+  }
+}
+
+// v * exp(sign * 2*pi*i * K / D), sign = -1 forward; trivial and 45-degree
+// roots take the short forms.
+template <int K, int D, bool fwd>
+__device__ __forceinline__ float2 rot(float2 v) {
+  constexpr int k = ((K % D) + D) % D;
+  if constexpr (k == 0) {
+    return v;
+  } else if constexpr (2 * k == D) {
+    return make_float2(-v.x, -v.y);
+  } else if constexpr (4 * k == D || 4 * k == 3 * D) {
+    // exp(-i pi/2) = -i forward; the inverse and the 3/4 turn flip it
+    constexpr bool minus_i = (4 * k == D) == fwd;
+    return minus_i ? make_float2(v.y, -v.x) : make_float2(-v.y, v.x);
+  } else {
+    constexpr CRoot w = croot(k, D);
+    constexpr float c = float(w.c), s = fwd ? float(-w.s) : float(w.s);
+    if constexpr ((8 * k) % D == 0) {
+      // |c| = |s| = sqrt(1/2)
+      constexpr float a = c > 0 ? 0.70710678118654752f : -0.70710678118654752f;
+      constexpr bool same = (c > 0) == (s > 0);
+      return same ? make_float2(a * (v.x - v.y), a * (v.x + v.y)) : make_float2(a * (v.x + v.y), a * (v.y - v.x));
+    } else {
+      return make_float2(fmaf(v.x, c, -v.y * s), fmaf(v.x, s, v.y * c));
+    }
+  }
+}
+
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 cmulf(float2 a, float2 w) {
+  return make_float2(fmaf(a.x, w.x, -a.y * w.y), fmaf(a.x, w.y, a.y * w.x));
+}
+
+// ---- R-point DFT in registers (radix-2 DIF; X[k] ends in v[brev<R>(k)]) ---
+template <int L, bool fwd, int I>
+__device__ __forceinline__ void dif_bfly(float2* v) {
+  constexpr int k = I % L, p = (I / L) * 2 * L + k;
+  const float2 a = v[p], b = v[p + L];
+  v[p] = cadd(a, b);
+  v[p + L] = rot<k, 2 * L, fwd>(csub(a, b));
+}
+template <int L, bool fwd, int... I>
+__device__ __forceinline__ void dif_stage(float2* v, std::integer_sequence<int, I...>) {
+  (dif_bfly<L, fwd, I>(v), ...);
+}
+template <int R, int L, bool fwd>
+__device__ __forceinline__ void dif_stages(float2* v) {
+  dif_stage<L, fwd>(v, std::make_integer_sequence<int, R / 2>{});
+  if constexpr (L > 1) dif_stages<R, L / 2, fwd>(v);
+}
+template <int R, bool fwd>
+__device__ __forceinline__ void dft(float2* v) {
+  if constexpr (R > 1) dif_stages<R, R / 2, fwd>(v);
+}
+
+template <int R>
+__host__ __device__ constexpr int brev(int k) {
+  int r = 0;
+  for (int m = R; m > 1; m >>= 1) {
+    r = (r << 1) | (k & 1);
+    k >>= 1;
+  }
+  return r;
+}
+
+// v[0..R) from bit-reversed to natural order (register renaming only).
+template <int R>
+__device__ __forceinline__ void unscramble(float2* v) {
+  float2 tmp[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) tmp[r] = v[brev<R>(r)];
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = tmp[r];
+}
+
+// exp(sign * 2*pi*i * num / den), den a power of two, exact argument.
+template <bool fwd>
+__device__ __forceinline__ float2 root(int num, int den) {
   float s, c;
-  sincospif(2.0f * float(num % den) / float(den), &s, &c);
-  return make_float2(c, forward ? -s : s);
+  sincospif(float(num & (den - 1)) * (2.0f / float(den)), &s, &c);
+  return make_float2(c, fwd ? -s : s);
 }
 
-// One Stockham pass of radix R over `count` signals of length N held in
-// `ws`: butterfly j (< N/R) of each signal reads x[j + r*N/R], applies
-// w_{Ns*R}^{r*(j mod Ns)}, transforms, and writes y[(j/Ns)*Ns*R + j%Ns + r*Ns].
-template <typename T, int N, int R, int P, int COUNT, bool forward>
-__device__ __forceinline__ void stockham_pass(vec2_t<T>* ws, int Ns, int t) {
-  constexpr int BF = N * COUNT / R;  // butterflies in the tile
-  constexpr int PER = (BF + P - 1) / P;
-  float2 v[PER][R];
+// w[r] = exp(sign * 2*pi*i * r*km / den) for r < R: powers of one sincospif
+// root, re-anchored by another sincospif every 8 powers.
+template <int R, bool fwd>
+__device__ __forceinline__ void root_powers(float2* w, int km, int den) {
+  constexpr int A = R < 8 ? R : 8;
+  w[0] = make_float2(1.0f, 0.0f);
+  if constexpr (R > 1) w[1] = root<fwd>(km, den);
 #pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int b = t + P * q;
-    if (b < BF) {
-      const int sig = b / (N / R), j = b % (N / R);
+  for (int r = 2; r < A; ++r) w[r] = cmulf(w[r - 1], w[1]);
 #pragma unroll
-      for (int r = 0; r < R; ++r) v[q][r] = to_f2<T>(ws[sig * N + j + r * (N / R)]);
+  for (int a = 1; a < R / 8; ++a) {
+    const float2 anchor = root<fwd>(8 * a * km, den);
+    w[8 * a] = anchor;
+#pragma unroll
+    for (int b = 1; b < 8; ++b) w[8 * a + b] = cmulf(anchor, w[b]);
+  }
+}
+
+// Workspace layout of one exchange: element p at p + (p >> kPad) (kPad = 0:
+// no padding).  kPad >= 4 stays inside (N + pad_h(N)) * batch elements.
+template <int kPad>
+__device__ __forceinline__ int xidx(int p) {
+  if constexpr (kPad == 0) return p;
+  else return p + (p >> kPad);
+}
+
+// Radix plan and exchange layouts per N (register-file bound: M = N/P
+// elements of each signal per thread in the first and last pass).
+template <int N>
+struct plan;
+template <> struct plan<64>   { static constexpr int n = 3, R[4] = {2, 16, 2, 0},  pad8[3] = {4, 4, 0}, pad4[3] = {4, 4, 0}; };
+template <> struct plan<128>  { static constexpr int n = 3, R[4] = {4, 8, 4, 0},   pad8[3] = {4, 4, 0}, pad4[3] = {5, 4, 0}; };
+template <> struct plan<256>  { static constexpr int n = 4, R[4] = {2, 8, 8, 2},   pad8[3] = {4, 4, 0}, pad4[3] = {5, 5, 0}; };
+template <> struct plan<512>  { static constexpr int n = 3, R[4] = {16, 2, 16, 0}, pad8[3] = {4, 0, 0}, pad4[3] = {5, 0, 0}; };
+template <> struct plan<1024> { static constexpr int n = 2, R[4] = {32, 32, 0, 0}, pad8[3] = {5, 0, 0}, pad4[3] = {5, 0, 0}; };
+template <> struct plan<2048> { static constexpr int n = 3, R[4] = {32, 2, 32, 0}, pad8[3] = {5, 0, 0}, pad4[3] = {5, 0, 0}; };
+template <> struct plan<4096> { static constexpr int n = 3, R[4] = {32, 4, 32, 0}, pad8[3] = {5, 0, 0}, pad4[3] = {5, 0, 0}; };
+
+template <typename T, int N>
+__host__ __device__ constexpr int exchange_pad(int x) {
+  return sizeof(vec2_t<T>) == 8 ? plan<N>::pad8[x] : plan<N>::pad4[x];
+}
+
+// Pass s of the plan over the thread's EPT registers.  Butterfly q = t + P*h
+// (h < EPT/R) of the tile is (signal b = q / NB, j = q % NB), NB = N/R; it
+// reads x[b][j + r*NB], multiplies input r by w^r with
+// w = W_{Ns*R}^{j mod Ns} (j mod Ns = t mod Ns because Ns divides P), and
+// writes X[b][(j/Ns)*Ns*R + j%Ns + r*Ns].  The first pass (Ns = 1) reads the
+// fragment; the last (Ns*R = N, NB = P) leaves its outputs in the fragment.
+template <typename T, int N, int EPT, int P, bool fwd, int s, int Ns>
+__device__ __forceinline__ void run_passes(float2* v, vec2_t<T>* ws, int t) {
+  using Pl = plan<N>;
+  constexpr int R = Pl::R[s], NB = N / R, C = EPT / R;
+  constexpr bool first = s == 0, last = s == Pl::n - 1;
+  if constexpr (!first) {
+    constexpr int padin = exchange_pad<T, N>(s - 1);
+#pragma unroll
+    for (int h = 0; h < C; ++h) {
+      const int q = t + P * h, b = q / NB, j = q % NB;
+#pragma unroll
+      for (int r = 0; r < R; ++r) v[h * R + r] = to_f2<T>(ws[xidx<padin>(b * N + j + r * NB)]);
+    }
+    float2 w[R];
+    root_powers<R, fwd>(w, t & (Ns - 1), Ns * R);
+#pragma unroll
+    for (int h = 0; h < C; ++h) {
+#pragma unroll
+      for (int r = 1; r < R; ++r) v[h * R + r] = cmulf(v[h * R + r], w[r]);
     }
   }
-  __syncthreads();
 #pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int b = t + P * q;
-    if (b < BF) {
-      const int sig = b / (N / R), j = b % (N / R);
-      const int k = j % Ns;
+  for (int h = 0; h < C; ++h) dft<R, fwd>(v + h * R);
+  if constexpr (last) {
 #pragma unroll
-      for (int r = 1; r < R; ++r) v[q][r] = cmul(v[q][r], unit_root(r * k, Ns * R, forward));
-      float2 o[R];
-      if constexpr (R == 2) {
-        o[0] = make_float2(v[q][0].x + v[q][1].x, v[q][0].y + v[q][1].y);
-        o[1] = make_float2(v[q][0].x - v[q][1].x, v[q][0].y - v[q][1].y);
-      } else {
-        const float2 t0 = make_float2(v[q][0].x + v[q][2].x, v[q][0].y + v[q][2].y);
-        const float2 t1 = make_float2(v[q][0].x - v[q][2].x, v[q][0].y - v[q][2].y);
-        const float2 t2 = make_float2(v[q][1].x + v[q][3].x, v[q][1].y + v[q][3].y);
-        const float2 d = make_float2(v[q][1].x - v[q][3].x, v[q][1].y - v[q][3].y);
-        // w4 * d with w4 = -i (forward) or +i (inverse)
-        const float2 t3 = forward ? make_float2(d.y, -d.x) : make_float2(-d.y, d.x);
-        o[0] = make_float2(t0.x + t2.x, t0.y + t2.y);
-        o[2] = make_float2(t0.x - t2.x, t0.y - t2.y);
-        o[1] = make_float2(t1.x + t3.x, t1.y + t3.y);
-        o[3] = make_float2(t1.x - t3.x, t1.y - t3.y);
-      }
-      const int dst = (j / Ns) * Ns * R + k;
+    for (int h = 0; h < C; ++h) unscramble<R>(v + h * R);
+  } else {
+    constexpr int padout = exchange_pad<T, N>(s);
+    __syncthreads();  // every thread's reads of the workspace are done
 #pragma unroll
-      for (int r = 0; r < R; ++r) ws[sig * N + dst + r * Ns] = from_f2<T>(o[r]);
+    for (int h = 0; h < C; ++h) {
+      const int q = t + P * h, b = q / NB, j = q % NB;
+      const int base = b * N + (j / Ns) * Ns * R + (j % Ns);
+#pragma unroll
+      for (int r = 0; r < R; ++r) ws[xidx<padout>(base + r * Ns)] = from_f2<T>(v[h * R + brev<R>(r)]);
     }
+    __syncthreads();
+    run_passes<T, N, EPT, P, fwd, s + 1, Ns * R>(v, ws, t);
   }
-  __syncthreads();
 }
 
-template <typename T, int N, int COUNT, bool forward, int P>
-__device__ __forceinline__ void stockham_fft(vec2_t<T>* ws, int t) {
-  int Ns = 1;
-  constexpr int L = LOG2P_builtin<N>;
-#pragma unroll
-  for (int p = 0; p < L / 2; ++p) {
-    stockham_pass<T, N, 4, P, COUNT, forward>(ws, Ns, t);
-    Ns *= 4;
-  }
-  if constexpr (L % 2 == 1) stockham_pass<T, N, 2, P, COUNT, forward>(ws, Ns, t);
-}
-
+}  // namespace dfft
 }  // namespace detail
 
 template <typename T, int N, int batch, bool forward>
@@ -109,14 +263,16 @@ __device__ __forceinline__ void ThunderFFT_kernel_reg(vec2_t<T>* __restrict__ re
                 "Unsupported ThunderFFT length");
   (void)W;
   using F = detail::frag<N, batch>;
+  static_assert(F::EPT % (N / F::P) == 0, "fragment must hold whole first-pass butterflies");
   vec2_t<T>* ws = static_cast<vec2_t<T>*>(workspace);
   const int t = detail::block_thread();
+  float2 v[F::EPT];
 #pragma unroll
-  for (int i = 0; i < F::EPT; ++i) ws[t + F::P * i] = reg[i];
-  __syncthreads();
-  detail::stockham_fft<T, N, batch, forward, F::P>(ws, t);
+  for (int i = 0; i < F::EPT; ++i) v[i] = detail::to_f2<T>(reg[i]);
+  detail::dfft::run_passes<T, N, F::EPT, F::P, forward, 0, 1>(v, ws, t);
+  __syncthreads();  // the workspace is the caller's again
 #pragma unroll
-  for (int i = 0; i < F::EPT; ++i) reg[i] = ws[t + F::P * i];
+  for (int i = 0; i < F::EPT; ++i) reg[i] = detail::from_f2<T>(v[i]);
 }
 
 }  // namespace thunderfft

@@ -20,7 +20,7 @@ def build(name: str, force: bool = False) -> Path:
     lib = libbuild.build()
     src = HERE / f"{name}.cu"
     exe = OUT / name
-    headers = list((ROOT / "include").rglob("*.h*"))
+    headers = [p for p in (ROOT / "include").rglob("*") if p.suffix in (".h", ".cuh", ".hpp")]
     if not force and exe.exists() and all(p.stat().st_mtime <= exe.stat().st_mtime for p in [src, lib, *headers]):
         return exe
     OUT.mkdir(exist_ok=True)

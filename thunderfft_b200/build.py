@@ -60,7 +60,7 @@ def build_paper_fft(force: bool = False) -> Path:
     of the library links it (header + -lthunderfft_b200, plus cuFFT for its
     accuracy check)."""
     lib = build()
-    headers = list((ROOT / "include").rglob("*.h*"))
+    headers = [p for p in (ROOT / "include").rglob("*") if p.suffix in (".h", ".cuh", ".hpp")]
     if (not force and PAPER_FFT.exists() and
             all(p.stat().st_mtime <= PAPER_FFT.stat().st_mtime for p in [PAPER_FFT_SRC, lib, *headers])):
         return PAPER_FFT
