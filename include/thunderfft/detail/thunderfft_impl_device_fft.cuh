@@ -20,8 +20,10 @@
 // 256: 2|8|8|2, 512: 16|2|16, 1024: 32|32, 2048: 32|2|32, 4096: 32|4|32.
 // Register DFTs are radix-2 decimation in frequency with compile-time roots;
 // inter-pass twiddles come from a few exact sincospif anchors (every 8th
-// power) and short power chains.  half data is widened to FP32 on entry,
-// rounded to half2 in the workspace exchanges and on exit.
+// power) and depth-3 product trees, or from compile-time roots where a
+// thread's twiddle base takes only two values.  Workspace accesses are a
+// per-thread base plus compile-time offsets.  half data is widened to FP32
+// on entry, rounded to half2 in the workspace exchanges and on exit.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -162,21 +164,41 @@ __device__ __forceinline__ float2 root(int num, int den) {
   return make_float2(c, fwd ? -s : s);
 }
 
-// w[r] = exp(sign * 2*pi*i * r*km / den) for r < R: powers of one sincospif
-// root, re-anchored by another sincospif every 8 powers.
-template <int R, bool fwd>
-__device__ __forceinline__ void root_powers(float2* w, int km, int den) {
-  constexpr int A = R < 8 ? R : 8;
-  w[0] = make_float2(1.0f, 0.0f);
-  if constexpr (R > 1) w[1] = root<fwd>(km, den);
+template <int K, int D, bool fwd>
+__device__ __forceinline__ float2 croot_f2() {
+  constexpr CRoot w = croot(K, D);
+  return make_float2(float(w.c), fwd ? float(-w.s) : float(w.s));
+}
+template <int D, bool fwd, int... I>
+__device__ __forceinline__ void select_powers(float2* w, bool odd, std::integer_sequence<int, I...>) {
+  ((w[I] = odd ? croot_f2<I, D, fwd>() : make_float2(1.0f, 0.0f)), ...);
+}
+
+// w[r] = exp(sign * 2*pi*i * r*km / den) for r < R.  km < 2: compile-time
+// roots selected per thread.  Otherwise one exact sincospif root, powers
+// 2..7 by a depth-3 product tree, and another sincospif anchor every 8
+// powers.
+template <int R, int Ns, bool fwd>
+__device__ __forceinline__ void root_powers(float2* w, int km) {
+  constexpr int den = Ns * R;
+  if constexpr (Ns == 2) {
+    select_powers<den, fwd>(w, km != 0, std::make_integer_sequence<int, R>{});
+  } else {
+    w[0] = make_float2(1.0f, 0.0f);
+    if constexpr (R > 1) w[1] = root<fwd>(km, den);
+    if constexpr (R > 2) w[2] = cmulf(w[1], w[1]);
+    if constexpr (R > 3) w[3] = cmulf(w[2], w[1]);
+    if constexpr (R > 4) w[4] = cmulf(w[2], w[2]);
+    if constexpr (R > 5) w[5] = cmulf(w[4], w[1]);
+    if constexpr (R > 6) w[6] = cmulf(w[4], w[2]);
+    if constexpr (R > 7) w[7] = cmulf(w[4], w[3]);
 #pragma unroll
-  for (int r = 2; r < A; ++r) w[r] = cmulf(w[r - 1], w[1]);
+    for (int a = 1; a < R / 8; ++a) {
+      const float2 anchor = root<fwd>(8 * a * km, den);
+      w[8 * a] = anchor;
 #pragma unroll
-  for (int a = 1; a < R / 8; ++a) {
-    const float2 anchor = root<fwd>(8 * a * km, den);
-    w[8 * a] = anchor;
-#pragma unroll
-    for (int b = 1; b < 8; ++b) w[8 * a + b] = cmulf(anchor, w[b]);
+      for (int b = 1; b < 8; ++b) w[8 * a + b] = cmulf(anchor, w[b]);
+    }
   }
 }
 
@@ -205,27 +227,42 @@ __host__ __device__ constexpr int exchange_pad(int x) {
   return sizeof(vec2_t<T>) == 8 ? plan<N>::pad8[x] : plan<N>::pad4[x];
 }
 
-// Pass s of the plan over the thread's EPT registers.  Butterfly q = t + P*h
-// (h < EPT/R) of the tile is (signal b = q / NB, j = q % NB), NB = N/R; it
-// reads x[b][j + r*NB], multiplies input r by w^r with
-// w = W_{Ns*R}^{j mod Ns} (j mod Ns = t mod Ns because Ns divides P), and
-// writes X[b][(j/Ns)*Ns*R + j%Ns + r*Ns].  The first pass (Ns = 1) reads the
-// fragment; the last (Ns*R = N, NB = P) leaves its outputs in the fragment.
+// Workspace positions of pass (R, Ns): butterfly q = t + P*h is (signal
+// b = q / NB, j = q % NB), NB = N/R; it reads x[b][j + r*NB] and writes
+// X[b][(j/Ns)*Ns*R + j%Ns + r*Ns].  With t < P and every factor a power of
+// two, both positions are bit-field concatenations of t's bits and (h, r)'s
+// bits, so index(t, h, r) = index(t, 0, 0) | index(0, h, r) and xidx splits
+// the same way: each access is a per-thread base plus a compile-time offset.
+template <int N, int P, int R>
+__host__ __device__ constexpr int rd_index(int t, int h, int r) {
+  return ((t + P * h) / (N / R)) * N + (t + P * h) % (N / R) + r * (N / R);
+}
+template <int N, int P, int R, int Ns>
+__host__ __device__ constexpr int wr_index(int t, int h, int r) {
+  const int q = t + P * h, j = q % (N / R);
+  return (q / (N / R)) * N + (j / Ns) * Ns * R + j % Ns + r * Ns;
+}
+
+// Pass s of the plan over the thread's EPT registers.  Input r of a
+// butterfly is multiplied by w^r, w = W_{Ns*R}^{j mod Ns} (j mod Ns =
+// t mod Ns because Ns divides P).  The first pass (Ns = 1) reads the
+// fragment; the last (Ns*R = N, NB = P, j = t) leaves its outputs in the
+// fragment.
 template <typename T, int N, int EPT, int P, bool fwd, int s, int Ns>
 __device__ __forceinline__ void run_passes(float2* v, vec2_t<T>* ws, int t) {
   using Pl = plan<N>;
-  constexpr int R = Pl::R[s], NB = N / R, C = EPT / R;
+  constexpr int R = Pl::R[s], C = EPT / R;
   constexpr bool first = s == 0, last = s == Pl::n - 1;
   if constexpr (!first) {
     constexpr int padin = exchange_pad<T, N>(s - 1);
+    const vec2_t<T>* src = ws + xidx<padin>(rd_index<N, P, R>(t, 0, 0));
 #pragma unroll
     for (int h = 0; h < C; ++h) {
-      const int q = t + P * h, b = q / NB, j = q % NB;
 #pragma unroll
-      for (int r = 0; r < R; ++r) v[h * R + r] = to_f2<T>(ws[xidx<padin>(b * N + j + r * NB)]);
+      for (int r = 0; r < R; ++r) v[h * R + r] = to_f2<T>(src[xidx<padin>(rd_index<N, P, R>(0, h, r))]);
     }
     float2 w[R];
-    root_powers<R, fwd>(w, t & (Ns - 1), Ns * R);
+    root_powers<R, Ns, fwd>(w, t & (Ns - 1));
 #pragma unroll
     for (int h = 0; h < C; ++h) {
 #pragma unroll
@@ -239,13 +276,13 @@ __device__ __forceinline__ void run_passes(float2* v, vec2_t<T>* ws, int t) {
     for (int h = 0; h < C; ++h) unscramble<R>(v + h * R);
   } else {
     constexpr int padout = exchange_pad<T, N>(s);
+    vec2_t<T>* dst = ws + xidx<padout>(wr_index<N, P, R, Ns>(t, 0, 0));
     __syncthreads();  // every thread's reads of the workspace are done
 #pragma unroll
     for (int h = 0; h < C; ++h) {
-      const int q = t + P * h, b = q / NB, j = q % NB;
-      const int base = b * N + (j / Ns) * Ns * R + (j % Ns);
 #pragma unroll
-      for (int r = 0; r < R; ++r) ws[xidx<padout>(base + r * Ns)] = from_f2<T>(v[h * R + brev<R>(r)]);
+      for (int r = 0; r < R; ++r)
+        dst[xidx<padout>(wr_index<N, P, R, Ns>(0, h, r))] = from_f2<T>(v[h * R + brev<R>(r)]);
     }
     __syncthreads();
     run_passes<T, N, EPT, P, fwd, s + 1, Ns * R>(v, ws, t);

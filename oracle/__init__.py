@@ -193,7 +193,7 @@ def ref_available() -> bool:
 
 def ref_sample(name: str) -> Path:
     """Path of a reference sample binary built by oracle/build_ref.py
-    (ref_conv1d_tiled, ref_conv1d_full); may not exist."""
+    (ref_conv1d_tiled, ref_conv1d_full, ref_paper_fft); may not exist."""
     return HERE / "_ref" / name
 
 

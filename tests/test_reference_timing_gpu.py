@@ -105,3 +105,32 @@ def test_fused_conv1d_vs_reference_sample(cuda):
     print(f"\n| fused conv1d, 16384 signals -> 4096 | ours (fp32 in/out, config 4) {ours:.1f} us "
           f"| reference sample (fp16 in/out, 4096-sample inputs) {ref:.1f} us | ratio {ref / ours:.2f}x |")
     assert ours > 0 and ref > 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("prec", ["tf32", "fp16"])
+def test_device_api_paper_fft_vs_reference(cuda, prec):
+    """Device API (ThunderFFT_kernel_reg in registers, repeated in one kernel)
+    through each library's paper_fft CLI, same arguments and CSV columns
+    (sample/bench/paper_fft.cu:159-185): compute_us is column 9, rel_l2
+    column 11.  Both must pass the 5e-3 gate."""
+    from thunderfft_b200 import build as libbuild
+
+    ref = oracle.ref_sample("ref_paper_fft")
+    if not ref.exists():
+        pytest.skip(f"{ref} not built")
+    ours = libbuild.build_paper_fft()
+    print(f"\n{'N':>5} {prec:>5}  ours_us  ref_us  ours_relL2  ref_relL2")
+    for n in (64, 128, 256, 512, 1024, 2048, 4096):
+        rows = []
+        for exe in (ours, ref):
+            out = subprocess.run([str(exe), str(n), prec, "register", "200", "2", "16384"], capture_output=True,
+                                 text=True, timeout=300)
+            assert out.returncode == 0, out.stderr[-2000:]
+            cols = out.stdout.strip().splitlines()[-1].split(",")
+            rows.append((float(cols[8]), float(cols[10])))
+        (ou, oe), (ru, re_) = rows
+        print(f"{n:>5} {prec:>5} {ou:8.2f} {ru:7.2f}  {oe:.2e}  {re_:.2e}")
+        assert oe <= 5e-3 and re_ <= 5e-3
+        if prec == "tf32":
+            assert oe <= 1e-5  # FP32 arithmetic on this side
