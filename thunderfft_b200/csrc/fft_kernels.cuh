@@ -710,9 +710,15 @@ struct Dft1Cfg {
   static constexpr int B_BYTES = 2 * N * 2 * N * ESZ;
   static constexpr int KSTEPS = 2 * N / D::kMmaK;
   static constexpr int SIN = kHalf ? 4 : 2;
+  // float2 C2C: outputs leave through two dedicated 16 KB staging slabs (one
+  // 32-column chunk each) so an input slot is free as soon as its MMAs end;
+  // half2 and window mode stage into the input slot they came from.
+  static constexpr int STG_BYTES = T * 128;
+  static constexpr int NSTG = kHalf ? 0 : 2;
   static constexpr uint32_t OFF_B = 0;
   static constexpr uint32_t OFF_IN = B_BYTES;
-  static constexpr uint32_t SMEM_BYTES = exclusive_smem(OFF_IN + SIN * TILE_BYTES + 1024);
+  static constexpr uint32_t OFF_STG = OFF_IN + SIN * TILE_BYTES;
+  static constexpr uint32_t SMEM_BYTES = exclusive_smem(OFF_STG + NSTG * STG_BYTES + 1024);
   static_assert(SMEM_BYTES + 512 <= 232448, "shared memory budget");
   static constexpr int kThreads = 192;                   // producer, MMA, 4 epilogue warps
 };
@@ -727,7 +733,11 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN];
   __shared__ uint64_t bar_acc_full[2], bar_acc_empty[2], bar_staged[2], bar_const, bar_done;
+  __shared__ uint64_t bar_stg_full[2], bar_stg_free[2];
   __shared__ uint32_t tmem_slot;
+  // separate output staging (float2 C2C, TMA store available): the MMA thread
+  // releases each input slot by tcgen05.commit when the slot's MMAs are done
+  const bool sep = !C::kIsHalf && !kWin && use_tma_store;
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const long long batch = p.batch;
@@ -738,6 +748,7 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
     for (int i = 0; i < C::SIN; ++i) { mbar_init(&bar_in_full[i], 1); mbar_init(&bar_in_empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar_acc_full[i], 1); mbar_init(&bar_acc_empty[i], 4); mbar_init(&bar_staged[i], 4);
+      mbar_init(&bar_stg_full[i], 4); mbar_init(&bar_stg_free[i], 1);
     }
     mbar_init(&bar_const, 1);
     mbar_init(&bar_done, 1);
@@ -861,6 +872,7 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
           else umma_tf32(d, ad, bd, idesc, k > 0);
         }
         umma_commit(&bar_acc_full[buf]);
+        if (sep) umma_commit(&bar_in_empty[slot]);
       }
       umma_commit(&bar_done);
       mbar_wait(&bar_done, 0, p.err, kDevTimeoutMma);
@@ -870,7 +882,56 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
     // epilogue: warp -> quadrant q = warp & 3, thread = signal 32q + lane
     const uint32_t q = warp & 3u;
     int pending_slot = -1;
-    for (int i = 0; i < my_tiles; ++i) {
+    if (sep) {
+      // Chunk g = 4 i + c (32 accumulator columns = 16 outputs of each of the
+      // tile's signals) goes through staging slab g & 1: every warp waits for
+      // the slab to be free, writes its 32 rows and arrives on stg_full; warp
+      // 2 lane 0 stores the slab (box {32, T, 1}) and, once the store of chunk
+      // g - 1 has read its slab, frees that one.
+      const int sig = (int)(32 * q + lane);
+      bool ok = true;
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        const long long tile = blockIdx.x + (long long)i * gridDim.x;
+        const int buf = i & 1;
+        if (!mbar_wait_warp(&bar_acc_full[buf], (uint32_t)(i >> 1) & 1u, p.err, kDevTimeoutEpilogue)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int chunk = 0; chunk < 4; ++chunk) {
+          const int g = 4 * i + chunk, sb = g & 1;
+          const uint32_t use = (uint32_t)(g >> 1);
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem + ((32u * q) << 16) + (uint32_t)(buf * 128 + chunk * 32), r);
+          tmem_wait_ld();
+          if (chunk == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_acc_empty[buf]);
+          }
+          if (!mbar_wait_warp(&bar_stg_free[sb], (use & 1u) ^ 1u, p.err, kDevTimeoutEpilogue)) { ok = false; break; }
+          const uint32_t sbase = smem_u32(smem + C::OFF_STG + sb * C::STG_BYTES);
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            st_shared_v4(sbase + sw128((uint32_t)sig * 128u + 16u * v), r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_stg_full[sb]);
+          if (warp == 2 && lane == 0) {
+            if (mbar_wait(&bar_stg_full[sb], use & 1u, p.err, kDevTimeoutEpilogue)) {
+              tma_store_3d(&tmap_out, smem + C::OFF_STG + sb * C::STG_BYTES, 0, (int)(tile * C::T), chunk);
+              bulk_commit_group();
+              bulk_wait_group_read<1>();   // chunk g - 1's store has read its slab
+              if (g >= 1) mbar_arrive(&bar_stg_free[sb ^ 1]);
+            } else {
+              ok = false;
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+          if (!ok) break;
+        }
+      }
+      if (warp == 2 && lane == 0) bulk_wait_group<0>();
+    }
+    for (int i = 0; !sep && i < my_tiles; ++i) {
       const long long tile = blockIdx.x + (long long)i * gridDim.x;
       const int slot = i % C::SIN, buf = i & 1;
       if (!mbar_wait_warp(&bar_acc_full[buf], (uint32_t)(i >> 1) & 1u, p.err, kDevTimeoutEpilogue)) break;
@@ -970,7 +1031,7 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
       }
       __syncwarp();
     }
-    if (warp == 2 && lane == 0) {
+    if (!sep && warp == 2 && lane == 0) {
       if (use_tma_store) bulk_wait_group<0>();   // (window mode: bulk stores)
       if (pending_slot >= 0) mbar_arrive(&bar_in_empty[pending_slot]);
     }

@@ -399,10 +399,13 @@ thff_status launch_dft1(DeviceState& st, const Consts& c, const void* in, void* 
   const uint64_t dims[3] = {uint64_t(C::E), uint64_t(batch), uint64_t(C::KATOMS)};
   const uint64_t strides[2] = {uint64_t(2 * C::N * C::ESZ), 128};
   const uint32_t box[3] = {uint32_t(C::E), uint32_t(C::T), uint32_t(C::KATOMS)};
+  // float2 stores one 32-column chunk (one K atom) per TMA store, half2 the tile
+  const uint32_t box_out[3] = {uint32_t(C::E), uint32_t(C::T), kHalf ? uint32_t(C::KATOMS) : 1u};
   const CUtensorMapDataType dt = kHalf ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   thff_status s;
   if (use_tma && (s = encode(&map_in, dt, 3, in, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) != THFF_OK) return s;
-  if (tma_store && (s = encode(&map_out, dt, 3, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) != THFF_OK) return s;
+  if (tma_store && (s = encode(&map_out, dt, 3, out, dims, strides, box_out, CU_TENSOR_MAP_SWIZZLE_128B)) != THFF_OK)
+    return s;
   thff::FftParams p;
   p.in = in; p.out = out; p.a1 = c.a1; p.a2 = nullptr; p.tw = nullptr;
   p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = st.d_err;
