@@ -132,12 +132,14 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_baseline(seconds: float = 12.0, sample_batch: int = 2048):
+def cpu_baseline(seconds: float = 12.0, sample_batch: int = 0):
     """FP64 oracle FFT (fwd + inv) on the host cores over a bounded sample of
-    the same workload; reported in the metric's unit (GB/s of algorithmic
-    bytes).  TEST INFRASTRUCTURE: the oracle is the checker/baseline only."""
+    the same workload (a quarter of the per-GPU batch, as in the reference
+    arm); reported in the metric's unit (GB/s of algorithmic bytes).  TEST
+    INFRASTRUCTURE: the oracle is the checker/baseline only."""
     import oracle
 
+    sample_batch = sample_batch or max(1, BATCH // 4)
     threads = oracle.hardware_threads()
     rng = np.random.default_rng(7)
     x = (rng.uniform(-1, 1, (sample_batch, N)) + 1j * rng.uniform(-1, 1, (sample_batch, N))).astype(np.complex64)
@@ -273,7 +275,9 @@ def run_reference(args):
     import oracle
 
     threads = oracle.hardware_threads()
-    sample_batch = 1024
+    # a quarter of the per-GPU batch per step: tens of milliseconds of CPU
+    # work, so thread start-up and clock ramp do not dominate a short run
+    sample_batch = max(1, BATCH // 4)
     rng = np.random.default_rng(7)
     x = (rng.uniform(-1, 1, (sample_batch, N)) + 1j * rng.uniform(-1, 1, (sample_batch, N))).astype(np.complex64)
     for _ in range(args.warmup):
@@ -287,7 +291,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3 * (BATCH / sample_batch),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "C2C fwd+inv, N=1024, batch 65536 per GPU (bounded CPU sample of 1024 signals)",
+        "config": {"workload": f"C2C fwd+inv, N={N}, batch {BATCH} per GPU (bounded CPU sample of {sample_batch} signals)",
                    "n": N, "batch_per_gpu": BATCH, "storage": "float2"},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} steps x (fwd+inv) of {sample_batch} signals, FP64 oracle"},
