@@ -22,8 +22,14 @@
 // inter-pass twiddles come from a few exact sincospif anchors (every 8th
 // power) and depth-3 product trees, or from compile-time roots where a
 // thread's twiddle base takes only two values.  Workspace accesses are a
-// per-thread base plus compile-time offsets.  half data is widened to FP32
-// on entry, rounded to half2 in the workspace exchanges and on exit.
+// per-thread base plus compile-time offsets.
+//
+// half2 storage computes in packed FP16 (the half2/FP16 storage-arithmetic
+// pair): a thread's butterflies are processed two at a time, the real parts
+// of both in one half2 and the imaginary parts in another, so each half2
+// instruction advances two butterflies with the same twiddles.  A pass with
+// a single butterfly per thread (the radix-32 passes of N >= 1024) runs in
+// FP32 between half2 loads and stores.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -114,25 +120,90 @@ __device__ __forceinline__ float2 cmulf(float2 a, float2 w) {
   return make_float2(fmaf(a.x, w.x, -a.y * w.y), fmaf(a.x, w.y, a.y * w.x));
 }
 
+// ---- packed FP16: two complex values per (re, im) pair of half2 ----------
+// Lane 0 of both halves is one butterfly's value, lane 1 another's; every
+// half2 instruction advances both butterflies.
+struct HP {
+  half2 re, im;
+};
+
+// IEEE binary16 bits of x (round to nearest even); x is 0 or normal-range
+// (the roots of unity used here are >= sin(2*pi/4096) in magnitude).
+__host__ __device__ constexpr unsigned short half_bits(double x) {
+  if (x == 0.0) return 0;
+  const unsigned short sign = x < 0 ? 0x8000 : 0;
+  if (x < 0) x = -x;
+  int e = 0;
+  while (x >= 2.0) { x *= 0.5; ++e; }
+  while (x < 1.0) { x *= 2.0; --e; }
+  const double m = (x - 1.0) * 1024.0;
+  long long mi = (long long)m;
+  const double frac = m - double(mi);
+  if (frac > 0.5 || (frac == 0.5 && (mi & 1))) ++mi;
+  if (mi == 1024) { mi = 0; ++e; }
+  return (unsigned short)(sign | (unsigned short)((e + 15) << 10) | (unsigned short)mi);
+}
+template <unsigned short B>
+__device__ __forceinline__ half2 hconst2() {
+  return __halves2half2(__ushort_as_half(B), __ushort_as_half(B));
+}
+
+__device__ __forceinline__ HP cadd(HP a, HP b) { return HP{__hadd2(a.re, b.re), __hadd2(a.im, b.im)}; }
+__device__ __forceinline__ HP csub(HP a, HP b) { return HP{__hsub2(a.re, b.re), __hsub2(a.im, b.im)}; }
+// v * w, w the same root in both lanes
+__device__ __forceinline__ HP cmulh(HP v, HP w) {
+  return HP{__hfma2(v.re, w.re, __hneg2(__hmul2(v.im, w.im))), __hfma2(v.re, w.im, __hmul2(v.im, w.re))};
+}
+__device__ __forceinline__ HP hpack(half2 a, half2 b) { return HP{__lows2half2(a, b), __highs2half2(a, b)}; }
+__device__ __forceinline__ half2 hlo(HP v) { return __lows2half2(v.re, v.im); }
+__device__ __forceinline__ half2 hhi(HP v) { return __highs2half2(v.re, v.im); }
+__device__ __forceinline__ HP hbroadcast(float2 w) { return HP{__float2half2_rn(w.x), __float2half2_rn(w.y)}; }
+
+template <int K, int D, bool fwd>
+__device__ __forceinline__ HP rot(HP v) {
+  constexpr int k = ((K % D) + D) % D;
+  if constexpr (k == 0) {
+    return v;
+  } else if constexpr (2 * k == D) {
+    return HP{__hneg2(v.re), __hneg2(v.im)};
+  } else if constexpr (4 * k == D || 4 * k == 3 * D) {
+    constexpr bool minus_i = (4 * k == D) == fwd;
+    return minus_i ? HP{v.im, __hneg2(v.re)} : HP{__hneg2(v.im), v.re};
+  } else {
+    constexpr CRoot w = croot(k, D);
+    constexpr double c = w.c, s = fwd ? -w.s : w.s;
+    if constexpr ((8 * k) % D == 0) {
+      const half2 a = hconst2<half_bits(c > 0 ? 0.70710678118654752 : -0.70710678118654752)>();
+      constexpr bool same = (c > 0) == (s > 0);
+      return same ? HP{__hmul2(a, __hsub2(v.re, v.im)), __hmul2(a, __hadd2(v.re, v.im))}
+                  : HP{__hmul2(a, __hadd2(v.re, v.im)), __hmul2(a, __hsub2(v.im, v.re))};
+    } else {
+      const half2 hc = hconst2<half_bits(c)>(), hs = hconst2<half_bits(s)>();
+      return HP{__hfma2(v.re, hc, __hneg2(__hmul2(v.im, hs))), __hfma2(v.re, hs, __hmul2(v.im, hc))};
+    }
+  }
+}
+
 // ---- R-point DFT in registers (radix-2 DIF; X[k] ends in v[brev<R>(k)]) ---
-template <int L, bool fwd, int I>
-__device__ __forceinline__ void dif_bfly(float2* v) {
+// V is float2 (FP32) or HP (two complex values in packed FP16).
+template <int L, bool fwd, int I, typename V>
+__device__ __forceinline__ void dif_bfly(V* v) {
   constexpr int k = I % L, p = (I / L) * 2 * L + k;
-  const float2 a = v[p], b = v[p + L];
+  const V a = v[p], b = v[p + L];
   v[p] = cadd(a, b);
   v[p + L] = rot<k, 2 * L, fwd>(csub(a, b));
 }
-template <int L, bool fwd, int... I>
-__device__ __forceinline__ void dif_stage(float2* v, std::integer_sequence<int, I...>) {
+template <int L, bool fwd, typename V, int... I>
+__device__ __forceinline__ void dif_stage(V* v, std::integer_sequence<int, I...>) {
   (dif_bfly<L, fwd, I>(v), ...);
 }
-template <int R, int L, bool fwd>
-__device__ __forceinline__ void dif_stages(float2* v) {
+template <int R, int L, bool fwd, typename V>
+__device__ __forceinline__ void dif_stages(V* v) {
   dif_stage<L, fwd>(v, std::make_integer_sequence<int, R / 2>{});
   if constexpr (L > 1) dif_stages<R, L / 2, fwd>(v);
 }
-template <int R, bool fwd>
-__device__ __forceinline__ void dft(float2* v) {
+template <int R, bool fwd, typename V>
+__device__ __forceinline__ void dft(V* v) {
   if constexpr (R > 1) dif_stages<R, R / 2, fwd>(v);
 }
 
@@ -147,9 +218,9 @@ __host__ __device__ constexpr int brev(int k) {
 }
 
 // v[0..R) from bit-reversed to natural order (register renaming only).
-template <int R>
-__device__ __forceinline__ void unscramble(float2* v) {
-  float2 tmp[R];
+template <int R, typename V>
+__device__ __forceinline__ void unscramble(V* v) {
+  V tmp[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) tmp[r] = v[brev<R>(r)];
 #pragma unroll
@@ -205,7 +276,7 @@ __device__ __forceinline__ void root_powers(float2* w, int km) {
 // Workspace layout of one exchange: element p at p + (p >> kPad) (kPad = 0:
 // no padding).  kPad >= 4 stays inside (N + pad_h(N)) * batch elements.
 template <int kPad>
-__device__ __forceinline__ int xidx(int p) {
+__host__ __device__ constexpr int xidx(int p) {
   if constexpr (kPad == 0) return p;
   else return p + (p >> kPad);
 }
@@ -289,6 +360,121 @@ __device__ __forceinline__ void run_passes(float2* v, vec2_t<T>* ws, int t) {
   }
 }
 
+// half2 storage.  Passes whose thread owns C >= 2 butterflies run them in
+// pairs (m, m + C/2) in packed FP16; a pass with one butterfly per thread
+// (the radix-32 passes of N >= 1024) runs in FP32.  Same plan, positions and
+// barriers as run_passes.
+//
+// For N <= 512 (batch_per_block >= 2) the pair (m, m + C/2) is, in every
+// pass, the same position of signals b and b + B/2, so the workspace keeps
+// the pairs packed: a plane of (re_b, re_b+B/2) half2 values followed by a
+// plane of the imaginary parts, indexed by the lower signal's position.  Only
+// entry and exit then move between the fragment's (re, im) half2 and the
+// packed pairs.  Larger N exchange (re, im) half2 elements.
+template <int N, int B>
+__host__ __device__ constexpr bool packed_exchange() {
+  return B >= 2 && N <= 512;
+}
+
+template <int N, int B, int EPT, int P, bool fwd, int s, int Ns>
+__device__ __forceinline__ void run_passes_h(half2* reg, half2* ws, int t) {
+  using Pl = plan<N>;
+  constexpr int R = Pl::R[s], C = EPT / R;
+  constexpr bool first = s == 0, last = s == Pl::n - 1;
+  constexpr bool soa = packed_exchange<N, B>();
+  constexpr int padin = first ? 0 : exchange_pad<half, N>(s - 1);
+  constexpr int padout = last ? 0 : exchange_pad<half, N>(s);
+  // packed planes: imaginary plane after the padded real plane of B/2 signals
+  constexpr int PLin = soa ? xidx<padin>(B / 2 * N) : 0, PLout = soa ? xidx<padout>(B / 2 * N) : 0;
+  const half2* src = ws + xidx<padin>(rd_index<N, P, R>(t, 0, 0));
+  half2* dst = ws + xidx<padout>(wr_index<N, P, R, Ns>(t, 0, 0));
+  if constexpr (C >= 2) {
+    constexpr int CP = C / 2;
+    HP v[CP * R];
+#pragma unroll
+    for (int m = 0; m < CP; ++m) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if constexpr (first) {
+          v[m * R + r] = hpack(reg[m * R + r], reg[(m + CP) * R + r]);
+        } else if constexpr (soa) {
+          const int o = xidx<padin>(rd_index<N, P, R>(0, m, r));
+          v[m * R + r] = HP{src[o], src[PLin + o]};
+        } else {
+          v[m * R + r] = hpack(src[xidx<padin>(rd_index<N, P, R>(0, m, r))],
+                               src[xidx<padin>(rd_index<N, P, R>(0, m + CP, r))]);
+        }
+      }
+    }
+    if constexpr (!first) {
+      float2 w[R];
+      root_powers<R, Ns, fwd>(w, t & (Ns - 1));
+#pragma unroll
+      for (int r = 1; r < R; ++r) {
+        const HP wh = hbroadcast(w[r]);
+#pragma unroll
+        for (int m = 0; m < CP; ++m) v[m * R + r] = cmulh(v[m * R + r], wh);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < CP; ++m) dft<R, fwd>(v + m * R);
+    if constexpr (last) {
+#pragma unroll
+      for (int m = 0; m < CP; ++m) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          reg[m * R + r] = hlo(v[m * R + brev<R>(r)]);
+          reg[(m + CP) * R + r] = hhi(v[m * R + brev<R>(r)]);
+        }
+      }
+    } else {
+      __syncthreads();  // every thread's reads of the workspace are done
+#pragma unroll
+      for (int m = 0; m < CP; ++m) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const HP x = v[m * R + brev<R>(r)];
+          if constexpr (soa) {
+            const int o = xidx<padout>(wr_index<N, P, R, Ns>(0, m, r));
+            dst[o] = x.re;
+            dst[PLout + o] = x.im;
+          } else {
+            dst[xidx<padout>(wr_index<N, P, R, Ns>(0, m, r))] = hlo(x);
+            dst[xidx<padout>(wr_index<N, P, R, Ns>(0, m + CP, r))] = hhi(x);
+          }
+        }
+      }
+      __syncthreads();
+    }
+  } else {
+    static_assert(!soa, "packed exchanges need two butterflies per thread in every pass");
+    float2 v[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if constexpr (first) v[r] = __half22float2(reg[r]);
+      else v[r] = __half22float2(src[xidx<padin>(rd_index<N, P, R>(0, 0, r))]);
+    }
+    if constexpr (!first) {
+      float2 w[R];
+      root_powers<R, Ns, fwd>(w, t & (Ns - 1));
+#pragma unroll
+      for (int r = 1; r < R; ++r) v[r] = cmulf(v[r], w[r]);
+    }
+    dft<R, fwd>(v);
+    if constexpr (last) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) reg[r] = __floats2half2_rn(v[brev<R>(r)].x, v[brev<R>(r)].y);
+    } else {
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        dst[xidx<padout>(wr_index<N, P, R, Ns>(0, 0, r))] = __floats2half2_rn(v[brev<R>(r)].x, v[brev<R>(r)].y);
+      __syncthreads();
+    }
+  }
+  if constexpr (!last) run_passes_h<N, B, EPT, P, fwd, s + 1, Ns * R>(reg, ws, t);
+}
+
 }  // namespace dfft
 }  // namespace detail
 
@@ -303,13 +489,17 @@ __device__ __forceinline__ void ThunderFFT_kernel_reg(vec2_t<T>* __restrict__ re
   static_assert(F::EPT % (N / F::P) == 0, "fragment must hold whole first-pass butterflies");
   vec2_t<T>* ws = static_cast<vec2_t<T>*>(workspace);
   const int t = detail::block_thread();
-  float2 v[F::EPT];
+  if constexpr (std::is_same_v<T, half>) {
+    detail::dfft::run_passes_h<N, batch, F::EPT, F::P, forward, 0, 1>(reg, ws, t);
+  } else {
+    float2 v[F::EPT];
 #pragma unroll
-  for (int i = 0; i < F::EPT; ++i) v[i] = detail::to_f2<T>(reg[i]);
-  detail::dfft::run_passes<T, N, F::EPT, F::P, forward, 0, 1>(v, ws, t);
+    for (int i = 0; i < F::EPT; ++i) v[i] = reg[i];
+    detail::dfft::run_passes<T, N, F::EPT, F::P, forward, 0, 1>(v, ws, t);
+#pragma unroll
+    for (int i = 0; i < F::EPT; ++i) reg[i] = v[i];
+  }
   __syncthreads();  // the workspace is the caller's again
-#pragma unroll
-  for (int i = 0; i < F::EPT; ++i) reg[i] = detail::from_f2<T>(v[i]);
 }
 
 }  // namespace thunderfft
