@@ -82,6 +82,18 @@ thff_status thff_sync_check(void* stream);
  * trigger, or a CUDA error. */
 thff_status thff_selftest_wait_timeout(int limit_us, void* stream);
 
+/* Test hook for host-side fault injection (no counterpart in the reference,
+ * whose error path is tf_check_cuda, detail/util_cuda.h:20-24).  On the
+ * calling thread, the (skip+1)-th CUDA status this library checks after the
+ * call reads as `cuda_error` (a cudaError_t value).  The CUDA call itself has
+ * still run; only its reported status changes.  The entry point that meets it
+ * returns THFF_CUDA_ERROR with the message
+ * "[ThunderFFT] <what>: <cudaGetErrorString(cuda_error)>", which the C++
+ * header throws as std::runtime_error.  cuda_error = 0 disarms it.  Lets
+ * callers and tests exercise their CUDA-failure handling without making a
+ * GPU fail. */
+thff_status thff_test_inject_cuda_error(int cuda_error, int skip);
+
 /* ---- fused real 1-D FFT convolution --------------------------------------
  * Counterpart of the reference's fused conv1d sample
  * (sample/conv1d/conv1d_fullfft_l4096_thunder.cu:280-331), here for float

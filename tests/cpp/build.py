@@ -10,7 +10,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
 OUT = HERE / "_build"
-PROGRAMS = ("host_contract", "device_api", "cache_lifecycle")
+PROGRAMS = ("host_contract", "device_api", "cache_lifecycle", "cuda_error_contract")
 
 
 def build(name: str, force: bool = False) -> Path:

@@ -30,3 +30,46 @@ def test_selftest_argument_checks():
     lib = tf.load_library()
     assert lib.thff_selftest_wait_timeout(0, None) == tf.THFF_INVALID_ARGUMENT
     assert lib.thff_selftest_wait_timeout(2_000_000, None) == tf.THFF_INVALID_ARGUMENT
+
+
+def test_inject_hook_argument_checks():
+    import thunderfft_b200 as tf
+
+    lib = tf.load_library()
+    assert lib.thff_test_inject_cuda_error(-1, 0) == tf.THFF_INVALID_ARGUMENT
+    assert lib.thff_test_inject_cuda_error(2, -1) == tf.THFF_INVALID_ARGUMENT
+    assert lib.thff_test_inject_cuda_error(0, 0) == tf.THFF_OK
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("skip", [0, 1, 2])
+def test_injected_cuda_failure_surfaces_and_library_recovers(cuda, skip):
+    """Host-side fault injection: the (skip+1)-th CUDA status the library
+    checks reads as cudaErrorMemoryAllocation (2).  The Python mirror must
+    raise RuntimeError with the reference's message shape, only on the
+    calling thread, and the next call must work."""
+    import threading
+
+    import torch
+
+    import thunderfft_b200 as tf
+
+    lib = tf.load_library()
+    x = (np.random.default_rng(1).standard_normal((16, 1024)) + 0j).astype(np.complex64)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty_like(xd)
+    tf.ThunderFFT_global("float", 1024, True, xd, yd, 16)
+    # armed on another thread: this thread is unaffected
+    t = threading.Thread(target=lambda: lib.thff_test_inject_cuda_error(2, 0))
+    t.start()
+    t.join()
+    tf.ThunderFFT_global("float", 1024, True, xd, yd, 16)
+    assert lib.thff_test_inject_cuda_error(2, skip) == tf.THFF_OK
+    with pytest.raises(RuntimeError) as ei:
+        tf.ThunderFFT_global("float", 1024, True, xd, yd, 16)
+    lib.thff_test_inject_cuda_error(0, 0)
+    msg = str(ei.value)
+    assert msg.startswith("[ThunderFFT] ") and msg.endswith(": out of memory"), msg
+    yd.zero_()
+    tf.ThunderFFT_global("float", 1024, True, xd, yd, 16)
+    assert oracle.rel_l2(yd.cpu().numpy(), oracle.fft(x)) <= 5e-3

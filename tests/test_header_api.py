@@ -53,3 +53,14 @@ def test_cache_lifecycle_program(cuda):
     res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "checks passed" in res.stdout
+
+
+@pytest.mark.gpu
+def test_cuda_error_contract_program(cuda):
+    """A CUDA failure inside the header API throws std::runtime_error with the
+    reference's "[ThunderFFT] <what>: <cudaGetErrorString>" message and leaves
+    the library usable (failure injected on the host, no GPU fault)."""
+    exe = cppbuild.build("cuda_error_contract")
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "checks passed" in res.stdout

@@ -91,6 +91,8 @@ def load_library() -> ctypes.CDLL:
     lib.thff_conv2d.restype = i32
     lib.thff_selftest_wait_timeout.argtypes = [i32, vp]
     lib.thff_selftest_wait_timeout.restype = i32
+    lib.thff_test_inject_cuda_error.argtypes = [i32, i32]
+    lib.thff_test_inject_cuda_error.restype = i32
     lib.thff_conv1d_set_arithmetic.argtypes = [i32]
     lib.thff_conv1d_set_arithmetic.restype = i32
     lib.thff_conv1d_tiled_operator_bytes.argtypes = [i32]

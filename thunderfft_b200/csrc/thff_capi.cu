@@ -41,9 +41,28 @@ thff_status cuda_fail(cudaError_t e, const char* what) {
   return fail(THFF_CUDA_ERROR, std::string("[ThunderFFT] ") + what + ": " + cudaGetErrorString(e));
 }
 
+// Host-side fault injection (thff_test_inject_cuda_error): per calling
+// thread, the (skip+1)-th CUDA status checked through THFF_CUDA reads as the
+// armed error.  The CUDA call itself has run; only its reported status
+// changes, so the error paths above the C ABI can be exercised without
+// making a GPU fail.
+thread_local int g_inject_error = 0;
+thread_local int g_inject_skip = 0;
+
+cudaError_t injected(cudaError_t real) {
+  if (g_inject_error == 0) return real;
+  if (g_inject_skip > 0) {
+    --g_inject_skip;
+    return real;
+  }
+  const cudaError_t e = static_cast<cudaError_t>(g_inject_error);
+  g_inject_error = 0;
+  return e;
+}
+
 #define THFF_CUDA(expr, what)                      \
   do {                                             \
-    cudaError_t e_ = (expr);                       \
+    cudaError_t e_ = injected(expr);               \
     if (e_ != cudaSuccess) return cuda_fail(e_, what); \
   } while (0)
 
@@ -805,6 +824,13 @@ thff_status thff_selftest_wait_timeout(int limit_us, void* stream) {
   thff::wait_timeout_selftest_kernel<<<1, 32, 0, cs>>>(st->d_err, 1000ull * (unsigned long long)limit_us);
   THFF_CUDA(cudaGetLastError(), "selftest launch");
   return read_device_error(*st, cs);
+}
+
+thff_status thff_test_inject_cuda_error(int cuda_error, int skip) {
+  if (cuda_error < 0 || skip < 0) return fail(THFF_INVALID_ARGUMENT, "inject: error code and skip must be >= 0");
+  g_inject_error = cuda_error;
+  g_inject_skip = cuda_error == 0 ? 0 : skip;
+  return THFF_OK;
 }
 
 long long thff_conv1d_spectrum_bytes(int dtype, int n) {
