@@ -191,6 +191,19 @@ thff_status thff_conv2d(int dtype, long long batch, int channels, int h, int w, 
                         const void* d_spectra, void* d_y, void* d_workspace, long long workspace_bytes,
                         void* stream);
 
+/* Arithmetic of thff_conv2d[_async] (process-wide; no reference counterpart,
+ * the reference's conv2d sample is FP16 throughout).
+ *   THFF_CONV_TF32: float2 intermediates, TF32 tensor-core passes.
+ *   THFF_CONV_MIXED: half2 intermediates; the row pass reads the fp32 images
+ *     in TF32, the other three are FP16 passes with FP32 accumulation.  Exact
+ *     power-of-two scales chosen from bounds (per image pair from max|x|, per
+ *     call from max|H|) keep every half2 value at or below 2^9, so any finite
+ *     input stays in FP16 range; the last pass removes them.  It moves 10
+ *     instead of 16 bytes per pixel and image pair through HBM.
+ * The same workspace size serves both.  thff_conv2d_noalloc always uses
+ * THFF_CONV_TF32. */
+thff_status thff_conv2d_set_arithmetic(int mode);
+
 /* Allocation-free variant of thff_conv2d_async (no counterpart in the
  * reference).  For callers that cannot allocate device memory where they
  * convolve: work captured into a CUDA graph (cudaMalloc breaks stream

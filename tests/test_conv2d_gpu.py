@@ -9,6 +9,19 @@ import oracle
 GATE = 5e-3
 
 
+@pytest.fixture(params=["tf32", "mixed"])
+def arith(request):
+    """Both arithmetics of the 2-D convolution; restores the default."""
+    import thunderfft_b200 as tf
+
+    tf.conv2d_set_arithmetic(request.param)
+    yield request.param
+    tf.conv2d_set_arithmetic(DEFAULT_ARITH)
+
+
+DEFAULT_ARITH = "tf32"
+
+
 def run(torch, tf, x, filt, pairs_per_pass=None):
     B, C, h, w = x.shape
     dx = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
@@ -35,7 +48,7 @@ def reference(x, filt):
                                              # 4096 takes the transposing-store path)
                                              (3, 1, 1024, 2048, 5, None), (2, 2, 2048, 1024, 3, 1),
                                              (1, 1, 128, 4096, 3, None), (2, 1, 4096, 128, 3, None)])
-def test_conv2d_matches_direct_circular_convolution(cuda, B, C, h, w, f, pairs):
+def test_conv2d_matches_direct_circular_convolution(cuda, arith, B, C, h, w, f, pairs):
     import torch
 
     import thunderfft_b200 as tf
@@ -50,7 +63,7 @@ def test_conv2d_matches_direct_circular_convolution(cuda, B, C, h, w, f, pairs):
 
 
 @pytest.mark.gpu
-def test_config5_full_size(cuda):
+def test_config5_full_size(cuda, arith):
     """64 x 32 fp32 N(0,1) 512x512 images, 32 N(0,1) 31x31
     filters (one per channel), circular convolution; sampled images checked
     against the FP64 direct convolution."""
@@ -71,6 +84,27 @@ def test_config5_full_size(cuda):
         xs = x[b, c].cpu().double().numpy()[None]
         ref = oracle.circconv2d(xs, filt[c].cpu().double().numpy()[None], np.zeros(1, np.int32))
         assert oracle.rel_l2(y[b, c].cpu().numpy()[None], ref) <= GATE, (b, c)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("xscale,fscale", [(1e-7, 1.0), (3e4, 1.0), (1.0, 1e-6), (1.0, 5e3), (2e4, 2e3)])
+def test_conv2d_range_scaling(cuda, arith, xscale, fscale):
+    """Images and filters far from unit scale, plus one spike per image: the
+    mixed arithmetic's power-of-two scales keep every half2 intermediate in
+    range, so the result meets the same gate as for unit-scale data."""
+    import torch
+
+    import thunderfft_b200 as tf
+
+    B, C, h, w, f = 3, 2, 256, 512, 9
+    rng = np.random.default_rng(int(np.log10(xscale) * 10 + np.log10(fscale) * 100) & 0xffff)
+    x = (rng.standard_normal((B, C, h, w)) * xscale).astype(np.float32)
+    x[:, :, 7, 11] *= 50.0
+    filt = (rng.standard_normal((C, f, f)) * fscale).astype(np.float32)
+    y = run(torch, tf, x, filt)
+    assert np.isfinite(y).all()
+    e = oracle.rel_l2(y, reference(x, filt))
+    assert e <= GATE, e
 
 
 def test_conv2d_argument_contract():

@@ -34,7 +34,7 @@ __all__ = [
     "ThunderFFTInitialize", "ThunderFFTFinalize", "ThunderFFT_global", "c2c_async", "sync_check",
     "twiddle_table", "fft", "load_library", "library_path", "SUPPORTED_N", "batch_per_block",
     "warp_per_block", "threads_per_warp", "version", "conv1d_filter_spectrum", "conv1d",
-    "conv2d_filter_spectra", "conv2d", "conv2d_workspace", "conv1d_set_arithmetic",
+    "conv2d_filter_spectra", "conv2d", "conv2d_workspace", "conv1d_set_arithmetic", "conv2d_set_arithmetic",
     "conv1d_tiled_operator", "conv1d_tiled",
 ]
 
@@ -95,6 +95,8 @@ def load_library() -> ctypes.CDLL:
     lib.thff_test_inject_cuda_error.restype = i32
     lib.thff_conv1d_set_arithmetic.argtypes = [i32]
     lib.thff_conv1d_set_arithmetic.restype = i32
+    lib.thff_conv2d_set_arithmetic.argtypes = [i32]
+    lib.thff_conv2d_set_arithmetic.restype = i32
     lib.thff_conv1d_tiled_operator_bytes.argtypes = [i32]
     lib.thff_conv1d_tiled_operator_bytes.restype = i64
     lib.thff_conv1d_tiled_operator.argtypes = [i32, vp, i32, vp, vp]
@@ -310,6 +312,14 @@ def conv1d_set_arithmetic(mode) -> None:
     range scaling for stages 2-4, FP32 accumulation) or "tf32"."""
     code = {"mixed": CONV_MIXED, "tf32": CONV_TF32}.get(mode, mode)
     _check(load_library().thff_conv1d_set_arithmetic(int(code)))
+
+
+def conv2d_set_arithmetic(mode) -> None:
+    """Arithmetic of conv2d (process-wide): "tf32" (float2 intermediates) or
+    "mixed" (half2 intermediates with exact power-of-two range scaling, TF32
+    row pass on the fp32 images, FP16 passes with FP32 accumulation)."""
+    code = {"mixed": CONV_MIXED, "tf32": CONV_TF32}.get(mode, mode)
+    _check(load_library().thff_conv2d_set_arithmetic(int(code)))
 
 
 def conv2d_workspace(h: int, w: int, pairs: int, device=None):

@@ -97,20 +97,6 @@ __device__ __forceinline__ uint32_t acc_addr(uint32_t tmem, int s, uint32_t q, i
   }
 }
 
-// 2^e as a float, e clamped to [-120, 120] (exact).
-__device__ __forceinline__ float pow2f(int e) {
-  e = e < -120 ? -120 : (e > 120 ? 120 : e);
-  return __int_as_float((127 + e) << 23);
-}
-
-// ceil(log2(x)) for finite x > 0 (exact, from the bits; subnormals -> -126).
-__device__ __forceinline__ int ceil_log2f(float x) {
-  const uint32_t b = __float_as_uint(x);
-  const int e = (int)((b >> 23) & 0xffu);
-  if (e == 0) return -126;
-  return e - 127 + ((b & 0x7fffffu) ? 1 : 0);
-}
-
 }  // namespace detail
 
 // Shared state the epilogue warps use (pointers into the kernel's shared memory).

@@ -9,10 +9,13 @@
 // transform (z = x_b + i x_{b+1}; the filter is real, so Re/Im of the result
 // are the two outputs).  The four transform passes are fft2_kernel
 // instances with the conv2d input/output modes (fft_kernels.cuh); this file
-// holds the one-time filter-spectrum preparation.
+// holds the one-time filter-spectrum preparation and the range exponents of
+// the half2 (mixed-arithmetic) pipeline.
 #pragma once
 #include <cuda_runtime.h>
 #include <cstdint>
+
+#include "fft_kernels.cuh"
 
 namespace thff {
 
@@ -52,6 +55,63 @@ __global__ void conv2d_filter_cols_kernel(const double2* __restrict__ g, int C, 
   }
   const double scale = 1.0 / ((double)H * (double)W);
   spec[i] = make_float2((float)(sr * scale), (float)(si * scale));
+}
+
+// ---- range exponents of the half2 pipeline ------------------------------
+// Every half2 intermediate is kept at or below 2^9 per real or imaginary part,
+// so that inside a pass the stage-1 partial sums (at most NS * sqrt2 times
+// larger, NS <= 64) stay below the FP16 maximum 65504.  The bounds are exact
+// consequences of |DFT_n(v)| <= n max|v|, so no input overflows:
+//   P1 stores Y 2^e1,        e1 = 9 - ceil_log2(w sqrt2 max|x|)   per image pair
+//   P2 stores X H 2^e2,      e2 = -ceil_log2(2 h max|H|)           per call
+//   P3 stores Z 2^e3,        e3 = -ceil_log2(h sqrt2)              per call
+//   P4 multiplies by 2^-(e1 + e2 + e3).
+// The products get a 1e-4 relative margin against float rounding.
+
+// e1 of image pairs pair0 .. pair0 + gridDim.x - 1 into e1_out[blockIdx.x].
+__global__ void conv2d_pair_exp_kernel(const float* __restrict__ x, long long nimg_b, int chans, long long ppc,
+                                       long long pair0, int h, int w, int* __restrict__ e1_out) {
+  const long long pg = pair0 + blockIdx.x;
+  const long long ch = pg / ppc, b = 2 * (pg - ch * ppc);
+  const long long hw4 = (long long)h * w / 4;
+  float m = 0.f;
+  for (int img = 0; img < 2; ++img) {
+    if (b + img >= nimg_b) break;
+    const float4* src = reinterpret_cast<const float4*>(x + ((b + img) * chans + ch) * hw4 * 4);
+    for (long long i = threadIdx.x; i < hw4; i += blockDim.x) {
+      const float4 v = __ldg(src + i);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+  }
+  __shared__ float red[32];
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (threadIdx.x == 0) {
+      const float bound = m * (float)w * 1.41421356f * 1.0001f;
+      e1_out[blockIdx.x] = m > 0.f ? 9 - detail::ceil_log2f(bound) : 0;
+    }
+  }
+}
+
+// Largest real or imaginary part of the spectra, as float bits (nonnegative
+// floats order like their bit patterns) into *amax (zeroed by the caller).
+__global__ void conv2d_spectra_absmax_kernel(const float* __restrict__ spec, long long count, unsigned* amax) {
+  float m = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < count; i += (long long)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(__ldg(spec + i)));
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(amax, __float_as_uint(m));
+}
+
+// e2, e3 of one call into e[0], e[1] from the spectra's largest part.
+__global__ void conv2d_call_exp_kernel(const unsigned* amax, int h, int* e) {
+  const float mh = __uint_as_float(*amax);
+  e[0] = mh > 0.f ? -detail::ceil_log2f(2.0f * (float)h * mh * 1.0001f) : 0;
+  e[1] = -detail::ceil_log2f((float)h * 1.41421356f * 1.0001f);
 }
 
 }  // namespace thff

@@ -143,7 +143,10 @@ struct Fft2Cfg {
   static constexpr uint32_t OFF_IN = OFF_A2 + (A2_BYTES + 1023) / 1024 * 1024;
   static constexpr uint32_t OFF_Y = OFF_IN + SIN * TILE_BYTES;
   static constexpr uint32_t OFF_H = OFF_Y + 2 * TILE_BYTES;   // spectrum tiles (kHSlots)
-  static constexpr uint32_t SMEM_DATA = OFF_H + HS * TILE_BYTES;
+  // a tile's spectrum rows: T * N complex fp32 values (the tile itself for
+  // float2 storage, twice its size for half2)
+  static constexpr int SPEC_BYTES = T * N * 8;
+  static constexpr uint32_t SMEM_DATA = OFF_H + HS * SPEC_BYTES;
   static constexpr uint32_t SMEM_BYTES = exclusive_smem(SMEM_DATA + 1024 /*align slack*/);
   static_assert(SMEM_BYTES + 512 <= 232448, "shared memory budget");
   static constexpr int EPW = S::EPW;                       // epilogue warps per TMEM lane quadrant
@@ -173,6 +176,12 @@ struct FftParams {
   long long nimg_b;      // B (images per channel)
   long long ppc;         // image pairs per channel = ceil(B / 2)
   int blk_log2;          // kEpiBlocked: log2 of the block width Cb
+  // Power-of-two range scaling of the half2 2-D convolution (null for every
+  // other use): conv_exp[0], [1] = call exponents e2, e3; conv_exp[2 + i] =
+  // exponent e1 of image pair pair0 + i.  The stage-2 epilogue multiplies its
+  // outputs by 2^e, e = conv_pass 1: e1, 2: e2, 3: e3, 4: -(e1 + e2 + e3).
+  const int* conv_exp;
+  int conv_pass;
   // Overlapping windows (dft1_kernel<C, true>, the tiled convolution): signal
   // w is window t = w % win_per_sig of sequence b = w / win_per_sig, i.e.
   // in[b][t*win_stride + n] (zero past in_len); only its first win_stride
@@ -210,6 +219,20 @@ enum InMode : int {
 };
 
 namespace detail {
+
+// 2^e as a float, e clamped to [-120, 120] (exact).
+__device__ __forceinline__ float pow2f(int e) {
+  e = e < -120 ? -120 : (e > 120 ? 120 : e);
+  return __int_as_float((127 + e) << 23);
+}
+
+// ceil(log2(x)) for finite x > 0 (exact, from the bits; subnormals -> -126).
+__device__ __forceinline__ int ceil_log2f(float x) {
+  const uint32_t b = __float_as_uint(x);
+  const int e = (int)((b >> 23) & 0xffu);
+  if (e == 0) return -126;
+  return e - 127 + ((b & 0x7fffffu) ? 1 : 0);
+}
 
 template <bool kHalf>
 __device__ __forceinline__ void store_complex(uint32_t saddr, float re, float im);
@@ -250,7 +273,10 @@ __device__ __forceinline__ uint32_t in_tile_offset(int sig, int s, int a) {
 // ---------------------------------------------------------------------------
 // Two-stage kernel
 // ---------------------------------------------------------------------------
-template <class C, int kEpi = kEpiNatural, int kIn = kInNatural>
+// kOutHalf: storage of the complex outputs (half2 or float2); it differs from
+// the configuration's storage only in the first pass of the half2 2-D
+// convolution (float2 input tile, half2 output).
+template <class C, int kEpi = kEpiNatural, int kIn = kInNatural, bool kOutHalf = C::kIsHalf>
 __global__ void __launch_bounds__(C::kThreads, 1)
 fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__ CUtensorMap tmap_spec,
             const FftParams p) {
@@ -374,8 +400,8 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
           const long long sig0 = tile * C::T;
           const long long img = sig0 / p.rows, r0 = sig0 - img * p.rows;
           const long long pg = p.pair0 + img, ch = pg / p.ppc;
-          mbar_arrive_expect_tx(&bar_h_full[hs], C::TILE_BYTES);
-          tma_load_3d(smem + C::OFF_H + hs * C::TILE_BYTES, &tmap_spec, &bar_h_full[hs], 0,
+          mbar_arrive_expect_tx(&bar_h_full[hs], C::SPEC_BYTES);
+          tma_load_3d(smem + C::OFF_H + hs * C::SPEC_BYTES, &tmap_spec, &bar_h_full[hs], 0,
                       (int)(((ch * p.rows + r0) * C::N) / 16), 0);
         }
         __syncwarp();
@@ -447,7 +473,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
     // (lanes 32q + 16*buf), the two warps split its 64-column chunks;
     // M=128: row blocks 2q, 2q+1 (lanes 32q, 32q+16), one per warp.
     // Each thread's twiddles are the same for every tile and are loaded once.
-    static_assert(kIn == kInNatural || !C::kIsHalf, "conv2d input modes are float storage only");
+    static_assert(kIn != kInPairPlanar || !C::kIsHalf, "the pair-planar input mode reads fp32 images");
     const uint32_t q = warp & 3u;
     const int h = (int)(warp - 2) >> 2;                 // warp index within its quadrant
     const int l = (int)(lane & 3u);
@@ -572,11 +598,12 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
       if constexpr (kStageH)
         if (!mbar_wait_warp(&bar_h_full[hs], (uint32_t)(i / C::HS) & 1u, p.err, kDevTimeoutEpilogue)) break;
       tc_fence_after();
-      const uint32_t hbase = smem_u32(smem + C::OFF_H + hs * C::TILE_BYTES);
+      const uint32_t hbase = smem_u32(smem + C::OFF_H + hs * C::SPEC_BYTES);
       const long long sig0 = tile * C::T;
       // conv2d modes: all T signals of a tile lie in one image (R % T == 0,
       // checked by the host), so the image bookkeeping is per tile.
       long long img = 0, r0 = 0;
+      float osc = 1.f;                  // range scale of the half2 2-D convolution (1 otherwise)
       const float2* spec_t = nullptr;   // kEpiMulNatural: spectrum rows of this tile
       float* y0 = nullptr;              // kEpiUnpackPair: output rows of images b, b+1
       float* y1 = nullptr;
@@ -585,6 +612,12 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
         r0 = sig0 - img * p.rows;
         const long long pg = p.pair0 + img, ch = pg / p.ppc, b = 2 * (pg - ch * p.ppc);
         if constexpr (kEpi == kEpiMulNatural) spec_t = p.spec + (ch * p.rows + r0) * C::N;
+        if (p.conv_exp) {
+          const int* e = p.conv_exp;
+          const int e1 = e[2 + (pg - p.pair0)];
+          const int se = p.conv_pass == 1 ? e1 : p.conv_pass == 2 ? e[0] : p.conv_pass == 3 ? e[1] : -(e1 + e[0] + e[1]);
+          osc = detail::pow2f(se);
+        }
         if constexpr (kEpi == kEpiUnpackPair) {
           y0 = reinterpret_cast<float*>(p.out) + ((b * p.chans + ch) * p.rows + r0) * C::N;
           if (b + 1 < p.nimg_b) y1 = y0 + (long long)p.chans * p.rows * C::N;
@@ -635,11 +668,108 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
             }
           }
         } else {
+        // half2 column-blocked output with Cb = 4 (one block row = 16 bytes):
+        // signal rows sl, sl+1 of one output k are neighbours in the layout,
+        // and a thread holds both (iterations j and j + NS/4).  Two quad
+        // shuffles per value let each lane store 8 bytes, so one store
+        // instruction writes whole 32-byte sectors.
+        constexpr bool kPairRows = kEpi == kEpiBlocked && kOutHalf && C::NS <= 16 && C::C2 % 2 == 0;
+        const bool pair_rows = kPairRows && p.blk_log2 == 2;
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
           uint32_t r[32];
           tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c) * 64, r);
           tmem_wait_ld();
+          if constexpr (kPairRows) {
+            if (pair_rows) {
+              constexpr int PJ = C::NS / 4;
+              const uint32_t l4 = lane & 3u, qbase = lane & ~3u;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if ((j / PJ) % 2 != 0) continue;
+                const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)l4;
+                const int c2 = pidx / C::NS, ks = pidx % C::NS;   // c2 even: rows sl, sl + 1
+                const int sl = g2 * C::C2 + c2;
+                const int k = C::NS * ka + ks;
+                uint32_t v[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const int jj = j + e * PJ;
+                  const float rr = __uint_as_float(r[4 * jj + 0]), ri = __uint_as_float(r[4 * jj + 1]);
+                  const float ir = __uint_as_float(r[4 * jj + 2]), ii = __uint_as_float(r[4 * jj + 3]);
+                  __half2 hh = __floats2half2_rn((rr - ii) * osc, (ir + ri) * osc);
+                  v[e] = *reinterpret_cast<uint32_t*>(&hh);
+                }
+                // lane l of the quad stores row sl + l/2, complex pair 2 (l%2), 2 (l%2) + 1
+                const uint32_t s0 = qbase + ((2u * l4) & 3u), s1 = qbase + ((2u * l4 + 1u) & 3u);
+                const uint32_t a0 = __shfl_sync(0xffffffffu, v[0], s0), b0 = __shfl_sync(0xffffffffu, v[1], s0);
+                const uint32_t a1 = __shfl_sync(0xffffffffu, v[0], s1), b1 = __shfl_sync(0xffffffffu, v[1], s1);
+                const bool first_row = l4 < 2u;
+                const int lb = 2;
+                const long long o = (((img * C::N + k) >> lb) * p.rows + r0 + sl + (first_row ? 0 : 1)) * 4 +
+                                    2 * (int)(l4 & 1u);
+                *reinterpret_cast<uint2*>(reinterpret_cast<uint32_t*>(p.out) + o) =
+                    make_uint2(first_row ? a0 : b0, first_row ? a1 : b1);
+              }
+              continue;
+            }
+          }
+          // 4-byte outputs along k (half2 spectrum products, fp32 image rows):
+          // iterations j and j + 1 hold outputs k and k + 4 of one signal, so
+          // the same quad shuffle gives each lane 8 contiguous bytes and the
+          // quad a whole 32-byte sector.  Conv-mode tiles are never partial.
+          // (Measured: it pays for the half2 spectrum products and the float2
+          // configurations' fp32 rows; the half2 configurations' fp32 rows,
+          // with one epilogue warp per lane quadrant, lose more to the
+          // shuffles than they gain.)
+          constexpr bool kPairK = ((kEpi == kEpiMulNatural && kOutHalf && kStageH) ||
+                                   (kEpi == kEpiUnpackPair && !C::kIsHalf)) && C::NS % 8 == 0;
+          if constexpr (kPairK) {
+            const uint32_t l4 = lane & 3u, qbase = lane & ~3u;
+            const uint32_t s0 = qbase + ((2u * l4) & 3u), s1 = qbase + ((2u * l4 + 1u) & 3u);
+            const bool first = l4 < 2u;
+            auto pair_store = [&](uint32_t* dst, uint32_t va, uint32_t vb) {
+              const uint32_t a0 = __shfl_sync(0xffffffffu, va, s0), b0 = __shfl_sync(0xffffffffu, vb, s0);
+              const uint32_t a1 = __shfl_sync(0xffffffffu, va, s1), b1 = __shfl_sync(0xffffffffu, vb, s1);
+              *reinterpret_cast<uint2*>(dst + 2 * l4) = make_uint2(first ? a0 : b0, first ? a1 : b1);
+            };
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+              const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)l4;
+              const int c2 = pidx / C::NS, ks = pidx % C::NS;    // ks % 8 < 4: k + 4 is this signal's too
+              const int sl = g2 * C::C2 + c2;
+              const int kq = C::NS * ka + ks - (int)l4;           // the quad's first output
+              float xr[2], xi[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int jj = j + e;
+                const float rr = __uint_as_float(r[4 * jj + 0]), ri = __uint_as_float(r[4 * jj + 1]);
+                const float ir = __uint_as_float(r[4 * jj + 2]), ii = __uint_as_float(r[4 * jj + 3]);
+                xr[e] = rr - ii;
+                xi[e] = ir + ri;
+              }
+              if constexpr (kEpi == kEpiMulNatural) {
+                uint32_t v[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const uint32_t byte = (uint32_t)(sl * C::N + kq + (int)l4 + 4 * e) * 8u;
+                  float2 w = ld_shared_v2f(hbase + (byte ^ (((byte >> 7) & 7u) << 4)));
+                  w.x *= osc;
+                  w.y *= osc;
+                  __half2 hh = __floats2half2_rn(xr[e] * w.x - xi[e] * w.y, xr[e] * w.y + xi[e] * w.x);
+                  v[e] = *reinterpret_cast<uint32_t*>(&hh);
+                }
+                pair_store(reinterpret_cast<uint32_t*>(p.out) + (sig0 + sl) * C::N + kq, v[0], v[1]);
+              } else {
+                pair_store(reinterpret_cast<uint32_t*>(y0 + sl * C::N + kq), __float_as_uint(xr[0] * osc),
+                           __float_as_uint(xr[1] * osc));
+                if (y1)
+                  pair_store(reinterpret_cast<uint32_t*>(y1 + sl * C::N + kq), __float_as_uint(xi[0] * osc),
+                             __float_as_uint(xi[1] * osc));
+              }
+            }
+            continue;
+          }
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)(lane & 3u);
@@ -650,8 +780,12 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
             if (sig0 + sl < batch) {
               const int k = C::NS * ka + ks;
               float xr = rr - ii, xi = ir + ri;
+              if constexpr (kEpi != kEpiNatural && kEpi != kEpiMulNatural) {
+                xr *= osc;
+                xi *= osc;
+              }
               if constexpr (kEpi == kEpiNatural) {
-                detail::store_out<C::kIsHalf>(p.out, (sig0 + sl) * C::N + k, xr, xi);
+                detail::store_out<kOutHalf>(p.out, (sig0 + sl) * C::N + k, xr, xi);
               } else if constexpr (kEpi == kEpiMulNatural) {
                 float2 w;
                 if constexpr (kStageH) {
@@ -661,11 +795,13 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
                 } else {
                   w = __ldg(spec_t + sl * C::N + k);
                 }
-                detail::store_out<C::kIsHalf>(p.out, (sig0 + sl) * C::N + k, xr * w.x - xi * w.y, xr * w.y + xi * w.x);
+                w.x *= osc;
+                w.y *= osc;
+                detail::store_out<kOutHalf>(p.out, (sig0 + sl) * C::N + k, xr * w.x - xi * w.y, xr * w.y + xi * w.x);
               } else if constexpr (kEpi == kEpiBlocked) {
                 const int lb = p.blk_log2;
                 const long long o = (((img * C::N + k) >> lb) * p.rows + r0 + sl) * (1LL << lb) + (k & ((1 << lb) - 1));
-                detail::store_out<C::kIsHalf>(p.out, o, xr, xi);
+                detail::store_out<kOutHalf>(p.out, o, xr, xi);
               } else {
                 // fp32 real outputs: Re -> image b, Im -> image b + 1
                 y0[sl * C::N + k] = xr;

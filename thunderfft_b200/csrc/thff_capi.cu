@@ -297,12 +297,13 @@ thff_status set_smem_attr(DeviceState& st, K kernel, int bytes) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Tensor map of a conv2d input mode (float storage).  Both modes deliver the
-// stage-1 tile in the MN-major [128-B column atom][K row][128 B] layout with
-// every box row one whole 128-B line; see thff::InMode for the column order.
+// Tensor map of a conv2d input mode.  Both modes deliver the stage-1 tile in
+// the MN-major [128-B column atom][K row][128 B] layout with every box row one
+// whole 128-B line; see thff::InMode for the column order.  The pair-planar
+// mode reads fp32 images; the column-blocked mode reads float2 or half2.
 template <class C, int kIn>
 thff_status encode_conv_input(CUtensorMap* map, const void* in, const thff::FftParams& ex, long long batch) {
-  static_assert(!C::kIsHalf, "conv2d input modes are float storage only");
+  static_assert(kIn != thff::kInPairPlanar || !C::kIsHalf, "the pair-planar mode reads fp32 images");
   uint64_t dims[5], strides[4];
   uint32_t box[5];
   if constexpr (kIn == thff::kInPairPlanar) {
@@ -327,19 +328,22 @@ thff_status encode_conv_input(CUtensorMap* map, const void* in, const thff::FftP
     // block, ex.rows signals per image, blocks consecutive across images);
     // n = a + NA s, a = a_lo + (16 / C1) a_hi: one 128-B line = 16 / C1
     // consecutive n of a block.  Shared memory [a_hi][g][s][line].
-    static_assert(16 % C::C1 == 0, "C1 divides a 128-B line");
-    constexpr uint64_t ALO = 16 / C::C1, AHI = C::NA / ALO;
-    const uint64_t blk = uint64_t(C::N) * C::C1 * 8, tiles = uint64_t(batch) / C::T;
-    const uint64_t d[5] = {32, uint64_t(C::NS), uint64_t(C::G1), AHI, tiles};
-    const uint64_t st[4] = {uint64_t(C::NA) * C::C1 * 8, blk, 128, uint64_t(C::G1) * blk};
-    const uint32_t b[5] = {32, uint32_t(C::NS), uint32_t(C::G1), uint32_t(AHI), 1};
+    // CPL complex values per 128-B line; elements of E = 2 CPL reals
+    constexpr uint64_t CSZ = 2 * C::ESZ, CPL = 128 / CSZ;
+    static_assert(CPL % C::C1 == 0, "C1 divides a 128-B line");
+    constexpr uint64_t ALO = CPL / C::C1, AHI = C::NA / ALO;
+    const uint64_t blk = uint64_t(C::N) * C::C1 * CSZ, tiles = uint64_t(batch) / C::T;
+    const uint64_t d[5] = {2 * CPL, uint64_t(C::NS), uint64_t(C::G1), AHI, tiles};
+    const uint64_t st[4] = {uint64_t(C::NA) * C::C1 * CSZ, blk, 128, uint64_t(C::G1) * blk};
+    const uint32_t b[5] = {uint32_t(2 * CPL), uint32_t(C::NS), uint32_t(C::G1), uint32_t(AHI), 1};
     std::memcpy(dims, d, sizeof d); std::memcpy(strides, st, sizeof st); std::memcpy(box, b, sizeof b);
   }
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, in, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+  return encode(map, C::kIsHalf ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, in, dims,
+                strides, box, C::kIsHalf ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
 template <bool kHalf, int kN, int kEpi = thff::kEpiNatural, int kIn = thff::kInNatural, int kVar = 0,
-          int kHS = 0>
+          int kHS = 0, bool kOutHalf = kHalf>
 thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* out, long long batch,
                         cudaStream_t stream, const thff::FftParams* extra = nullptr) {
   using C = thff::Fft2Cfg<kHalf, kN, kVar, kHS>;
@@ -386,7 +390,7 @@ thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* 
   CUtensorMap map_spec;
   std::memset(&map_spec, 0, sizeof(map_spec));
   if constexpr (kEpi == thff::kEpiMulNatural && kHS > 0) {
-    static_assert(!kHalf && (C::T * C::N) % 16 == 0 && C::T * C::N / 16 <= 256, "spectrum box");
+    static_assert((C::T * C::N) % 16 == 0 && C::T * C::N / 16 <= 256, "spectrum box");
     const uint64_t lines = uint64_t(p.chans) * uint64_t(p.rows) * C::N / 16;
     const uint64_t dims[3] = {32, lines, 1};
     const uint64_t strides[2] = {128, lines * 128};
@@ -396,7 +400,7 @@ thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* 
                            CU_TENSOR_MAP_SWIZZLE_128B);
     if (s != THFF_OK) return s;
   }
-  auto kernel = thff::fft2_kernel<C, kEpi, kIn>;
+  auto kernel = thff::fft2_kernel<C, kEpi, kIn, kOutHalf>;
   thff_status s = set_smem_attr(st, kernel, int(C::SMEM_BYTES));
   if (s != THFF_OK) return s;
   const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
@@ -528,6 +532,7 @@ thff_status launch_conv1d(DeviceState& st, const Consts& c, int lin, const void*
 // Arithmetic of the conv1d stages 2-4: THFF_CONV_MIXED (FP16 operands with
 // per-tile power-of-two range scaling) or THFF_CONV_TF32.
 std::atomic<int> g_conv1d_arith{THFF_CONV_MIXED};
+std::atomic<int> g_conv2d_arith{THFF_CONV_TF32};
 
 // Stage matrix + twiddles of the conv kernel: the forward DFT matrix of
 // length L = sqrt(n) (one group) and the forward twiddles of length n.
@@ -553,44 +558,46 @@ thff_status get_conv_consts(DeviceState& st, int n, const Consts** out) {
   return THFF_OK;
 }
 
-// Signals per stage-1 column group (C1) of the float FFT of length n: the
-// block width of the column-blocked layout that pass reads.
-int conv2d_c1(int n) {
+// Signals per stage-1 column group (C1) of the length-n FFT (float2 or half2
+// storage): the block width of the column-blocked layout that pass reads.
+int conv2d_c1(int n, bool half = false) {
   switch (n) {
-    case 128: return thff::Fft2Cfg<false, 128>::C1;
-    case 256: return thff::Fft2Cfg<false, 256>::C1;
-    case 512: return thff::Fft2Cfg<false, 512>::C1;
-    case 1024: return thff::Fft2Cfg<false, 1024>::C1;
-    case 2048: return thff::Fft2Cfg<false, 2048>::C1;
-    default: return thff::Fft2Cfg<false, 4096>::C1;
+    case 128: return half ? thff::Fft2Cfg<true, 128>::C1 : thff::Fft2Cfg<false, 128>::C1;
+    case 256: return half ? thff::Fft2Cfg<true, 256>::C1 : thff::Fft2Cfg<false, 256>::C1;
+    case 512: return half ? thff::Fft2Cfg<true, 512>::C1 : thff::Fft2Cfg<false, 512>::C1;
+    case 1024: return half ? thff::Fft2Cfg<true, 1024>::C1 : thff::Fft2Cfg<false, 1024>::C1;
+    case 2048: return half ? thff::Fft2Cfg<true, 2048>::C1 : thff::Fft2Cfg<false, 2048>::C1;
+    default: return half ? thff::Fft2Cfg<true, 4096>::C1 : thff::Fft2Cfg<false, 4096>::C1;
   }
 }
 
 // One pass of the 2-D convolution pipeline: length-n C2C transform of
-// `batch` signals with input mode kIn and stage-2 epilogue mode kEpi.
+// `batch` signals with input mode kIn and stage-2 epilogue mode kEpi, in
+// float2 (kHalf false) or half2 storage; kOutHalf: half2 outputs.
 // Spectrum staging slots of the length-n multiply pass: two when they fit
 // beside a 2-tile input ring, else one (computed without instantiating the
 // configuration that would not fit).
-template <int kN>
+template <bool kHalf, int kN>
 constexpr int conv2d_hslots() {
-  using B = thff::Fft2Cfg<false, kN>;
-  return (B::OFF_IN + (2 + 2 + 2) * B::TILE_BYTES + 1024 + 512 <= 232448u) ? 2 : 1;
+  using B = thff::Fft2Cfg<kHalf, kN>;
+  return (B::OFF_IN + (2 + 2) * B::TILE_BYTES + 2 * (B::T * B::N * 8) + 1024 + 512 <= 232448u) ? 2 : 1;
 }
 
-template <int kEpi, int kIn>
+template <int kEpi, int kIn, bool kHalf = false, bool kOutHalf = kHalf>
 thff_status conv2d_pass(DeviceState& st, const Consts& c, int n, const void* in, void* out, long long batch,
                         const thff::FftParams& extra, cudaStream_t cs) {
-  // the pair-planar pass uses the NA = 32 shape variant where one exists;
-  // the spectrum-multiply pass stages the spectrum tiles in shared memory
+  // the pair-planar pass uses the float NA = 32 shape variant where one
+  // exists; the spectrum-multiply pass stages the spectrum tiles in shared
+  // memory
   constexpr int kV = (kIn == thff::kInPairPlanar) ? 1 : 0;
   constexpr bool kMul = kEpi == thff::kEpiMulNatural;
   switch (n) {
-    case 128: return launch_fft2<false, 128, kEpi, kIn, kV, kMul ? conv2d_hslots<128>() : 0>(st, c, in, out, batch, cs, &extra);
-    case 256: return launch_fft2<false, 256, kEpi, kIn, kV, kMul ? conv2d_hslots<256>() : 0>(st, c, in, out, batch, cs, &extra);
-    case 512: return launch_fft2<false, 512, kEpi, kIn, kV, kMul ? conv2d_hslots<512>() : 0>(st, c, in, out, batch, cs, &extra);
-    case 1024: return launch_fft2<false, 1024, kEpi, kIn, 0, kMul ? conv2d_hslots<1024>() : 0>(st, c, in, out, batch, cs, &extra);
-    case 2048: return launch_fft2<false, 2048, kEpi, kIn, 0, kMul ? conv2d_hslots<2048>() : 0>(st, c, in, out, batch, cs, &extra);
-    case 4096: return launch_fft2<false, 4096, kEpi, kIn, 0, kMul ? conv2d_hslots<4096>() : 0>(st, c, in, out, batch, cs, &extra);
+    case 128: return launch_fft2<kHalf, 128, kEpi, kIn, kV, kMul ? conv2d_hslots<kHalf, 128>() : 0, kOutHalf>(st, c, in, out, batch, cs, &extra);
+    case 256: return launch_fft2<kHalf, 256, kEpi, kIn, kV, kMul ? conv2d_hslots<kHalf, 256>() : 0, kOutHalf>(st, c, in, out, batch, cs, &extra);
+    case 512: return launch_fft2<kHalf, 512, kEpi, kIn, kV, kMul ? conv2d_hslots<kHalf, 512>() : 0, kOutHalf>(st, c, in, out, batch, cs, &extra);
+    case 1024: return launch_fft2<kHalf, 1024, kEpi, kIn, 0, kMul ? conv2d_hslots<kHalf, 1024>() : 0, kOutHalf>(st, c, in, out, batch, cs, &extra);
+    case 2048: return launch_fft2<kHalf, 2048, kEpi, kIn, 0, kMul ? conv2d_hslots<kHalf, 2048>() : 0, kOutHalf>(st, c, in, out, batch, cs, &extra);
+    case 4096: return launch_fft2<kHalf, 4096, kEpi, kIn, 0, kMul ? conv2d_hslots<kHalf, 4096>() : 0, kOutHalf>(st, c, in, out, batch, cs, &extra);
   }
   return fail(THFF_INVALID_ARGUMENT, "conv2d: image sides must be in {128, ..., 4096}");
 }
@@ -637,6 +644,65 @@ thff_status conv2d_run(DeviceState& st, Lookup&& consts, long long nimg_b, int c
       return s;
     ex.rows = h;                     // P4: h row signals per image
     if ((s = conv2d_pass<thff::kEpiUnpackPair, thff::kInBlocked>(st, *row_i, w, z0, d_y, np * h, ex, cs)) != THFF_OK)
+      return s;
+  }
+  return THFF_OK;
+}
+
+// Mixed-arithmetic form of conv2d_run (THFF_CONV_MIXED): the intermediates
+// are half2.  P1 reads the fp32 images in TF32 and stores half2; P2-P4 are
+// FP16 passes with FP32 accumulation.  Power-of-two exponents
+// (conv2d_kernels.cuh) keep every half2 intermediate at or below 2^9 for any
+// finite input, and P4 undoes them.  Scratch: z0, z1 (chunk * h * w half2
+// each), e (2 + chunk ints), amax (one word).  consts_f finds the float
+// constants of P1, consts_h the half ones of P2-P4.
+template <class LookupF, class LookupH>
+thff_status conv2d_run_h(DeviceState& st, LookupF&& consts_f, LookupH&& consts_h, long long nimg_b, int chans,
+                         int h, int w, const void* d_x, const void* d_spectra, void* d_y, void* z0, void* z1, int* e,
+                         unsigned* amax, long long chunk, cudaStream_t cs) {
+  const Consts *row_f, *col_f, *col_i, *row_i;
+  thff_status s;
+  if ((s = consts_f(w, true, has_variant1(THFF_F32, w) ? 1 : 0, &row_f)) != THFF_OK ||
+      (s = consts_h(h, true, &col_f)) != THFF_OK || (s = consts_h(h, false, &col_i)) != THFF_OK ||
+      (s = consts_h(w, false, &row_i)) != THFF_OK)
+    return s;
+  const long long ppc = (nimg_b + 1) / 2, pairs = ppc * chans;
+  // call exponents e2, e3 from the spectra's largest part
+  THFF_CUDA(cudaMemsetAsync(amax, 0, sizeof(unsigned), cs), "conv2d range word");
+  thff::conv2d_spectra_absmax_kernel<<<unsigned(4 * st.sms), 256, 0, cs>>>(static_cast<const float*>(d_spectra),
+                                                                          2LL * chans * h * w, amax);
+  THFF_CUDA(cudaGetLastError(), "conv2d range launch");
+  thff::conv2d_call_exp_kernel<<<1, 1, 0, cs>>>(amax, h, e);
+  THFF_CUDA(cudaGetLastError(), "conv2d range launch");
+  thff::FftParams ex;
+  std::memset(&ex, 0, sizeof(ex));
+  ex.chans = chans; ex.nimg_b = nimg_b; ex.ppc = ppc; ex.spec = static_cast<const float2*>(d_spectra);
+  ex.conv_exp = e;
+  for (long long p0 = 0; p0 < pairs; p0 += chunk) {
+    const long long np = (pairs - p0 < chunk) ? pairs - p0 : chunk;
+    ex.pair0 = p0;
+    thff::conv2d_pair_exp_kernel<<<unsigned(np), 256, 0, cs>>>(static_cast<const float*>(d_x), nimg_b, chans, ppc,
+                                                                p0, h, w, e + 2);
+    THFF_CUDA(cudaGetLastError(), "conv2d range launch");
+    ex.rows = h;                     // P1: h row signals per image
+    ex.blk_log2 = ilog2(conv2d_c1(h, true));
+    ex.conv_pass = 1;
+    if ((s = conv2d_pass<thff::kEpiBlocked, thff::kInPairPlanar, false, true>(st, *row_f, w, d_x, z0, np * h, ex,
+                                                                               cs)) != THFF_OK)
+      return s;
+    ex.rows = w;                     // P2, P3: w column signals per image
+    ex.conv_pass = 2;
+    if ((s = conv2d_pass<thff::kEpiMulNatural, thff::kInBlocked, true>(st, *col_f, h, z0, z1, np * w, ex, cs)) !=
+        THFF_OK)
+      return s;
+    ex.blk_log2 = ilog2(conv2d_c1(w, true));
+    ex.conv_pass = 3;
+    if ((s = conv2d_pass<thff::kEpiBlocked, thff::kInNatural, true>(st, *col_i, h, z1, z0, np * w, ex, cs)) != THFF_OK)
+      return s;
+    ex.rows = h;                     // P4: h row signals per image
+    ex.conv_pass = 4;
+    if ((s = conv2d_pass<thff::kEpiUnpackPair, thff::kInBlocked, true>(st, *row_i, w, z0, d_y, np * h, ex, cs)) !=
+        THFF_OK)
       return s;
   }
   return THFF_OK;
@@ -942,6 +1008,13 @@ thff_status thff_conv1d_tiled(int dtype, long long input_len, int f, const void*
   return thff_sync_check(stream);
 }
 
+thff_status thff_conv2d_set_arithmetic(int mode) {
+  if (mode != THFF_CONV_MIXED && mode != THFF_CONV_TF32)
+    return fail(THFF_INVALID_ARGUMENT, "conv2d: arithmetic must be THFF_CONV_MIXED or THFF_CONV_TF32");
+  g_conv2d_arith.store(mode);
+  return THFF_OK;
+}
+
 thff_status thff_conv1d_set_arithmetic(int mode) {
   if (mode != THFF_CONV_MIXED && mode != THFF_CONV_TF32)
     return fail(THFF_INVALID_ARGUMENT, "conv1d: arithmetic must be THFF_CONV_MIXED or THFF_CONV_TF32");
@@ -991,8 +1064,8 @@ thff_status thff_conv2d_async(int dtype, long long nimg_b, int chans, int h, int
   if (!aligned16(d_x) || !aligned16(d_y) || !aligned16(d_workspace) || !aligned16(d_spectra))
     return fail(THFF_INVALID_ARGUMENT, "conv2d: buffers must be 16-byte aligned");
   const long long per_pair = 2LL * h * w * 8;
-  const long long chunk = workspace_bytes / per_pair;
-  if (chunk < 1) return fail(THFF_INVALID_ARGUMENT, "conv2d: workspace smaller than one image pair (2*h*w*16 bytes)");
+  if (workspace_bytes / per_pair < 1)
+    return fail(THFF_INVALID_ARGUMENT, "conv2d: workspace smaller than one image pair (2*h*w*16 bytes)");
   int dev;
   thff_status s = current_device(&dev);
   if (s != THFF_OK) return s;
@@ -1002,14 +1075,29 @@ thff_status thff_conv2d_async(int dtype, long long nimg_b, int chans, int h, int
     if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
   }
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  float2* z0 = static_cast<float2*>(d_workspace);
-  float2* z1 = z0 + (size_t)chunk * h * w;
   auto consts = [st](int n, bool fwd, int var, const Consts** c) -> thff_status {
     std::lock_guard<std::mutex> lock(g_mutex);
     return get_consts(*st, THFF_F32, n, fwd, c, var);
   };
-  return conv2d_run(*st, consts, nimg_b, chans, h, w, d_x, d_spectra, d_y, z0, z1, chunk,
-                    reinterpret_cast<cudaStream_t>(stream));
+  if (g_conv2d_arith.load() == THFF_CONV_MIXED) {
+    // half2 scratch: z0, z1 of chunk * h * w half2, then 2 + chunk exponents
+    // and the range word (the float workspace size always covers them)
+    const long long chunk = (workspace_bytes - 16) / (2LL * h * w * 4 + 4);
+    uint8_t* base = static_cast<uint8_t*>(d_workspace);
+    void* z0 = base;
+    void* z1 = base + chunk * h * w * 4;
+    int* e = reinterpret_cast<int*>(base + 2 * chunk * h * w * 4);
+    unsigned* amax = reinterpret_cast<unsigned*>(e + 2 + chunk);
+    auto consts_h = [st](int n, bool fwd, const Consts** c) -> thff_status {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      return get_consts(*st, THFF_F16, n, fwd, c, 0);
+    };
+    return conv2d_run_h(*st, consts, consts_h, nimg_b, chans, h, w, d_x, d_spectra, d_y, z0, z1, e, amax, chunk, cs);
+  }
+  const long long chunk = workspace_bytes / per_pair;
+  float2* z0 = static_cast<float2*>(d_workspace);
+  float2* z1 = z0 + (size_t)chunk * h * w;
+  return conv2d_run(*st, consts, nimg_b, chans, h, w, d_x, d_spectra, d_y, z0, z1, chunk, cs);
 }
 
 thff_status thff_conv2d(int dtype, long long nimg_b, int chans, int h, int w, const void* d_x, const void* d_spectra,
