@@ -191,8 +191,9 @@ thff_status thff_conv2d(int dtype, long long batch, int channels, int h, int w, 
                         const void* d_spectra, void* d_y, void* d_workspace, long long workspace_bytes,
                         void* stream);
 
-/* Arithmetic of thff_conv2d[_async] (process-wide; no reference counterpart,
- * the reference's conv2d sample is FP16 throughout).
+/* Arithmetic of thff_conv2d[_async] (process-wide, default THFF_CONV_MIXED;
+ * no reference counterpart, the reference's conv2d sample is FP16
+ * throughout).
  *   THFF_CONV_TF32: float2 intermediates, TF32 tensor-core passes.
  *   THFF_CONV_MIXED: half2 intermediates; the row pass reads the fp32 images
  *     in TF32, the other three are FP16 passes with FP32 accumulation.  Exact

@@ -19,7 +19,7 @@ def arith(request):
     tf.conv2d_set_arithmetic(DEFAULT_ARITH)
 
 
-DEFAULT_ARITH = "tf32"
+DEFAULT_ARITH = "mixed"
 
 
 def run(torch, tf, x, filt, pairs_per_pass=None):

@@ -315,9 +315,10 @@ def conv1d_set_arithmetic(mode) -> None:
 
 
 def conv2d_set_arithmetic(mode) -> None:
-    """Arithmetic of conv2d (process-wide): "tf32" (float2 intermediates) or
-    "mixed" (half2 intermediates with exact power-of-two range scaling, TF32
-    row pass on the fp32 images, FP16 passes with FP32 accumulation)."""
+    """Arithmetic of conv2d (process-wide): "mixed" (default: half2
+    intermediates with exact power-of-two range scaling, TF32 row pass on the
+    fp32 images, FP16 passes with FP32 accumulation) or "tf32" (float2
+    intermediates)."""
     code = {"mixed": CONV_MIXED, "tf32": CONV_TF32}.get(mode, mode)
     _check(load_library().thff_conv2d_set_arithmetic(int(code)))
 

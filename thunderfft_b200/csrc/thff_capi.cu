@@ -532,7 +532,7 @@ thff_status launch_conv1d(DeviceState& st, const Consts& c, int lin, const void*
 // Arithmetic of the conv1d stages 2-4: THFF_CONV_MIXED (FP16 operands with
 // per-tile power-of-two range scaling) or THFF_CONV_TF32.
 std::atomic<int> g_conv1d_arith{THFF_CONV_MIXED};
-std::atomic<int> g_conv2d_arith{THFF_CONV_TF32};
+std::atomic<int> g_conv2d_arith{THFF_CONV_MIXED};
 
 // Stage matrix + twiddles of the conv kernel: the forward DFT matrix of
 // length L = sqrt(n) (one group) and the forward twiddles of length n.
@@ -580,7 +580,11 @@ int conv2d_c1(int n, bool half = false) {
 template <bool kHalf, int kN>
 constexpr int conv2d_hslots() {
   using B = thff::Fft2Cfg<kHalf, kN>;
-  return (B::OFF_IN + (2 + 2) * B::TILE_BYTES + 2 * (B::T * B::N * 8) + 1024 + 512 <= 232448u) ? 2 : 1;
+  // the producer loads a tile's spectrum right after its input, so the
+  // spectrum slots bound how far it runs ahead: as many as fit, up to 4
+  for (int hs = 4; hs > 1; --hs)
+    if (B::OFF_IN + (2 + 2) * B::TILE_BYTES + hs * (B::T * B::N * 8) + 1024 + 512 <= 232448u) return hs;
+  return 1;
 }
 
 template <int kEpi, int kIn, bool kHalf = false, bool kOutHalf = kHalf>
