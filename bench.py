@@ -231,6 +231,7 @@ def sweep_conv1d(args, tf, dev, g, stream, timed, peak):
     """conv1d row of the sweep: BASELINE config 4 (batch / --sweep-scale)."""
     import torch
 
+    tf.conv1d_set_arithmetic(args.conv_arith)
     B1, lin, taps, n1 = 16384 // args.sweep_scale, 3072, 1025, 4096
     xs = torch.randn(B1, lin, device=dev, generator=g)
     hs = torch.randn(taps, device=dev, generator=g)
@@ -238,7 +239,7 @@ def sweep_conv1d(args, tf, dev, g, stream, timed, peak):
     ys = torch.empty(B1, n1, device=dev)
     us = timed(lambda: tf.conv1d(xs, spec, n1, out=ys, stream=stream, sync=False))
     alg = B1 * (lin + n1) * 4
-    print(f"| conv1d fp32 (config 4) | {n1} | {B1} x {lin} | fwd*H*inv | {us:.1f} | {alg / us / 1e3:.0f} | "
+    print(f"| conv1d fp32 (config 4), {args.conv_arith} | {n1} | {B1} x {lin} | fwd*H*inv | {us:.1f} | {alg / us / 1e3:.0f} | "
           f"{alg / us / 1e3 / peak:.3f} | |", flush=True)
 
 
@@ -246,6 +247,7 @@ def sweep_conv2d(args, tf, dev, g, stream, timed, peak):
     """conv2d row of the sweep: BASELINE config 5 (batch / --sweep-scale)."""
     import torch
 
+    tf.conv2d_set_arithmetic(args.conv_arith)
     B2, C2, hw, f = 64 // args.sweep_scale, 32, 512, 31
     xi = torch.randn(B2, C2, hw, hw, device=dev, generator=g)
     fi = torch.randn(C2, f, f, device=dev, generator=g)
@@ -254,7 +256,7 @@ def sweep_conv2d(args, tf, dev, g, stream, timed, peak):
     yi = torch.empty_like(xi)
     us = timed(lambda: tf.conv2d(xi, sp, ws, out=yi, stream=stream, sync=False))
     alg = 2 * xi.numel() * 4
-    print(f"| conv2d fp32 (config 5) | {hw}x{hw} | {B2} x {C2} | fwd*H*inv | {us:.1f} | {alg / us / 1e3:.0f} | "
+    print(f"| conv2d fp32 (config 5), {args.conv_arith} | {hw}x{hw} | {B2} x {C2} | fwd*H*inv | {us:.1f} | {alg / us / 1e3:.0f} | "
           f"{alg / us / 1e3 / peak:.3f} | |", flush=True)
 
 
@@ -316,6 +318,8 @@ def main():
                     help="print the per-size table (all N, both storage types, conv kernels) instead of the JSON line")
     ap.add_argument("--sweep-scale", type=int, default=1, help="divide the sweep's batches by this (profiling)")
     ap.add_argument("--no-conv", action="store_true", help="sweep: skip the conv1d / conv2d rows")
+    ap.add_argument("--conv-arith", default="mixed", choices=["mixed", "tf32"],
+                    help="sweep: arithmetic of the conv1d / conv2d rows (default: the library default, mixed)")
     ap.add_argument("--sweep-only", default="all", choices=["all", "fft", "conv1d", "conv2d"],
                     help="sweep: run only these rows (profiling one kernel)")
     args = ap.parse_args()
