@@ -90,6 +90,46 @@ def test_tiled_conv1d_vs_reference_sample(cuda):
 
 
 @pytest.mark.gpu
+def test_tiled_conv1d_small_vs_reference_sample(cuda):
+    """The sample's default size (2^16 elements, 10 tiles): launch-latency
+    bound, so ours is timed as GPU time per call by replaying 20 calls
+    captured in a CUDA graph (the sample reports its kernel time)."""
+    import torch
+
+    import thunderfft_b200 as tf
+
+    L, f = 1 << 16, 9
+    ref = _run_sample("ref_conv1d_tiled", [L, f, 0, 0, 5, 20], r"Kernel pipeline time:\s*([0-9.]+)\s*ms")
+    g = torch.randn(f, dtype=torch.complex64, device="cuda")
+    op = tf.conv1d_tiled_operator(g, "half")
+    x = torch.view_as_real(torch.randn(1, L, dtype=torch.complex64, device="cuda")).half().contiguous()
+    out = torch.empty(1, L - f + 1, 2, dtype=torch.float16, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            tf.conv1d_tiled(x, op, f, out=out, stream=s, sync=False)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        for _ in range(20):
+            tf.conv1d_tiled(x, op, f, out=out, stream=s, sync=False)
+    with torch.cuda.stream(s):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = _ev(torch), _ev(torch)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(10):
+            graph.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    ours = e0.elapsed_time(e1) / 200 * 1e3
+    print(f"\n| tiled conv1d half2, L=2^16, f=9 | ours {ours:.1f} us per call (graph replay) "
+          f"| reference sample kernel {ref:.1f} us | ratio {ref / ours:.2f}x |")
+    assert ours > 0 and ref > 0
+
+
+@pytest.mark.gpu
 def test_fused_conv1d_vs_reference_sample(cuda):
     import torch
 
