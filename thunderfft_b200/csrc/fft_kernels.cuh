@@ -603,7 +603,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
       // conv2d modes: all T signals of a tile lie in one image (R % T == 0,
       // checked by the host), so the image bookkeeping is per tile.
       long long img = 0, r0 = 0;
-      float osc = 1.f;                  // range scale of the half2 2-D convolution (1 otherwise)
+      float osc = 1.f, osc2 = 1.f;      // range scale osc * osc2 of the half2 2-D convolution (1 otherwise)
       const float2* spec_t = nullptr;   // kEpiMulNatural: spectrum rows of this tile
       float* y0 = nullptr;              // kEpiUnpackPair: output rows of images b, b+1
       float* y1 = nullptr;
@@ -616,7 +616,10 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
           const int* e = p.conv_exp;
           const int e1 = e[2 + (pg - p.pair0)];
           const int se = p.conv_pass == 1 ? e1 : p.conv_pass == 2 ? e[0] : p.conv_pass == 3 ? e[1] : -(e1 + e[0] + e[1]);
-          osc = detail::pow2f(se);
+          // two exact factors: |se| can exceed pow2f's +-120 (e1 reaches ~126
+          // for the smallest normal inputs) and stays within +-240
+          osc = detail::pow2f(se >> 1);
+          osc2 = detail::pow2f(se - (se >> 1));
         }
         if constexpr (kEpi == kEpiUnpackPair) {
           y0 = reinterpret_cast<float*>(p.out) + ((b * p.chans + ch) * p.rows + r0) * C::N;
@@ -697,7 +700,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
                   const int jj = j + e * PJ;
                   const float rr = __uint_as_float(r[4 * jj + 0]), ri = __uint_as_float(r[4 * jj + 1]);
                   const float ir = __uint_as_float(r[4 * jj + 2]), ii = __uint_as_float(r[4 * jj + 3]);
-                  __half2 hh = __floats2half2_rn((rr - ii) * osc, (ir + ri) * osc);
+                  __half2 hh = __floats2half2_rn((rr - ii) * osc * osc2, (ir + ri) * osc * osc2);
                   v[e] = *reinterpret_cast<uint32_t*>(&hh);
                 }
                 // lane l of the quad stores row sl + l/2, complex pair 2 (l%2), 2 (l%2) + 1
@@ -754,18 +757,18 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
                 for (int e = 0; e < 2; ++e) {
                   const uint32_t byte = (uint32_t)(sl * C::N + kq + (int)l4 + 4 * e) * 8u;
                   float2 w = ld_shared_v2f(hbase + (byte ^ (((byte >> 7) & 7u) << 4)));
-                  w.x *= osc;
-                  w.y *= osc;
+                  w.x = w.x * osc * osc2;
+                  w.y = w.y * osc * osc2;
                   __half2 hh = __floats2half2_rn(xr[e] * w.x - xi[e] * w.y, xr[e] * w.y + xi[e] * w.x);
                   v[e] = *reinterpret_cast<uint32_t*>(&hh);
                 }
                 pair_store(reinterpret_cast<uint32_t*>(p.out) + (sig0 + sl) * C::N + kq, v[0], v[1]);
               } else {
-                pair_store(reinterpret_cast<uint32_t*>(y0 + sl * C::N + kq), __float_as_uint(xr[0] * osc),
-                           __float_as_uint(xr[1] * osc));
+                pair_store(reinterpret_cast<uint32_t*>(y0 + sl * C::N + kq), __float_as_uint(xr[0] * osc * osc2),
+                           __float_as_uint(xr[1] * osc * osc2));
                 if (y1)
-                  pair_store(reinterpret_cast<uint32_t*>(y1 + sl * C::N + kq), __float_as_uint(xi[0] * osc),
-                             __float_as_uint(xi[1] * osc));
+                  pair_store(reinterpret_cast<uint32_t*>(y1 + sl * C::N + kq), __float_as_uint(xi[0] * osc * osc2),
+                             __float_as_uint(xi[1] * osc * osc2));
               }
             }
             continue;
@@ -781,8 +784,8 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
               const int k = C::NS * ka + ks;
               float xr = rr - ii, xi = ir + ri;
               if constexpr (kEpi != kEpiNatural && kEpi != kEpiMulNatural) {
-                xr *= osc;
-                xi *= osc;
+                xr = xr * osc * osc2;
+                xi = xi * osc * osc2;
               }
               if constexpr (kEpi == kEpiNatural) {
                 detail::store_out<kOutHalf>(p.out, (sig0 + sl) * C::N + k, xr, xi);
@@ -795,8 +798,8 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
                 } else {
                   w = __ldg(spec_t + sl * C::N + k);
                 }
-                w.x *= osc;
-                w.y *= osc;
+                w.x = w.x * osc * osc2;
+                w.y = w.y * osc * osc2;
                 detail::store_out<kOutHalf>(p.out, (sig0 + sl) * C::N + k, xr * w.x - xi * w.y, xr * w.y + xi * w.x);
               } else if constexpr (kEpi == kEpiBlocked) {
                 const int lb = p.blk_log2;
