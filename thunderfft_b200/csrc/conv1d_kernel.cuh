@@ -506,7 +506,12 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       if (lane == 0) {
-        e1_ring[i & 7] = (m > 0.f) ? 13 - detail::ceil_log2f(rb * m) : 0;
+        // clamped to pow2f's exact range (+-120) here, where every later use
+        // reads it, so the stage scales stay consistent.  (The final unscale
+        // -(e1 + e2 + e3) leaves that range only where the output itself is
+        // beyond float range.)
+        const int e1 = (m > 0.f) ? 13 - detail::ceil_log2f(rb * m) : 0;
+        e1_ring[i & 7] = e1 < -120 ? -120 : (e1 > 120 ? 120 : e1);
         mbar_arrive(&bar_scale[slot]);
         mbar_arrive(&bar_in_empty[slot]);
       }
