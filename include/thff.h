@@ -127,7 +127,10 @@ thff_status thff_conv1d(int dtype, int n, int lin, const void* d_x, const void* 
  *     significand as TF32) with FP32 accumulation; every FP16 operand is
  *     scaled by an exact power of two chosen from a bound on its magnitude
  *     (per tile for the stage-2 input, per call from max|H| for stage 3), so
- *     any finite fp32 input stays in FP16 range.
+ *     any finite fp32 input stays in FP16 range.  The output unscale is one
+ *     exact power of two while max|x| * max|H| <= 2^110 (outputs below
+ *     about 2^110); past that, near the top of fp32 range, use
+ *     THFF_CONV_TF32.
  *   THFF_CONV_TF32: all four stages TF32.
  * No reference counterpart (the reference's conv1d is FP16 only). */
 enum { THFF_CONV_MIXED = 0, THFF_CONV_TF32 = 1 };

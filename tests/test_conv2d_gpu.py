@@ -87,11 +87,16 @@ def test_config5_full_size(cuda, arith):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("xscale,fscale", [(1e-7, 1.0), (3e4, 1.0), (1.0, 1e-6), (1.0, 5e3), (2e4, 2e3)])
+@pytest.mark.parametrize(
+    "xscale,fscale",
+    [(1e-7, 1.0), (3e4, 1.0), (1.0, 1e-6), (1.0, 5e3), (2e4, 2e3), (1e-36, 1.0), (1e15, 1e15)],
+)
 def test_conv2d_range_scaling(cuda, arith, xscale, fscale):
     """Images and filters far from unit scale, plus one spike per image: the
     mixed arithmetic's power-of-two scales keep every half2 intermediate in
-    range, so the result meets the same gate as for unit-scale data."""
+    range, so the result meets the same gate as for unit-scale data.  The
+    (1e15, 1e15) case takes the last pass's unscale past 2^120 (applied as
+    two exact factors); (1e-36, 1) puts the image scale above 2^100."""
     import torch
 
     import thunderfft_b200 as tf

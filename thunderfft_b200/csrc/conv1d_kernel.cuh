@@ -508,8 +508,8 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
       if (lane == 0) {
         // clamped to pow2f's exact range (+-120) here, where every later use
         // reads it, so the stage scales stay consistent.  (The final unscale
-        // -(e1 + e2 + e3) leaves that range only where the output itself is
-        // beyond float range.)
+        // -(e1 + e2 + e3) <= log2(max|x| max|H|) + 10 stays in that range
+        // while max|x| max|H| <= 2^110.)
         const int e1 = (m > 0.f) ? 13 - detail::ceil_log2f(rb * m) : 0;
         e1_ring[i & 7] = e1 < -120 ? -120 : (e1 > 120 ? 120 : e1);
         mbar_arrive(&bar_scale[slot]);

@@ -92,7 +92,9 @@ __global__ void conv2d_pair_exp_kernel(const float* __restrict__ x, long long ni
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (threadIdx.x == 0) {
       const float bound = m * (float)w * 1.41421356f * 1.0001f;
-      e1_out[blockIdx.x] = m > 0.f ? 9 - detail::ceil_log2f(bound) : 0;
+      // clamped to pow2f's exact range: P1 scales by 2^e1 alone
+      const int e1 = m > 0.f ? 9 - detail::ceil_log2f(bound) : 0;
+      e1_out[blockIdx.x] = e1 < -120 ? -120 : (e1 > 120 ? 120 : e1);
     }
   }
 }
@@ -110,7 +112,9 @@ __global__ void conv2d_spectra_absmax_kernel(const float* __restrict__ spec, lon
 // e2, e3 of one call into e[0], e[1] from the spectra's largest part.
 __global__ void conv2d_call_exp_kernel(const unsigned* amax, int h, int* e) {
   const float mh = __uint_as_float(*amax);
-  e[0] = mh > 0.f ? -detail::ceil_log2f(2.0f * (float)h * mh * 1.0001f) : 0;
+  // clamped to pow2f's exact range: P2 scales by 2^e2 alone
+  const int e2 = mh > 0.f ? -detail::ceil_log2f(2.0f * (float)h * mh * 1.0001f) : 0;
+  e[0] = e2 < -120 ? -120 : (e2 > 120 ? 120 : e2);
   e[1] = -detail::ceil_log2f((float)h * 1.41421356f * 1.0001f);
 }
 

@@ -616,10 +616,16 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
           const int* e = p.conv_exp;
           const int e1 = e[2 + (pg - p.pair0)];
           const int se = p.conv_pass == 1 ? e1 : p.conv_pass == 2 ? e[0] : p.conv_pass == 3 ? e[1] : -(e1 + e[0] + e[1]);
-          // two exact factors: |se| can exceed pow2f's +-120 (e1 reaches ~126
-          // for the smallest normal inputs) and stays within +-240
-          osc = detail::pow2f(se >> 1);
-          osc2 = detail::pow2f(se - (se >> 1));
+          // e1, e2, e3 each lie within pow2f's exact range (+-120); the
+          // unscale -(e1 + e2 + e3) of the last pass can leave it for a
+          // representable output (inputs and spectra both large) and is
+          // applied as two exact factors there
+          if (kEpi == kEpiUnpackPair) {
+            osc = detail::pow2f(se >> 1);
+            osc2 = detail::pow2f(se - (se >> 1));
+          } else {
+            osc = detail::pow2f(se);
+          }
         }
         if constexpr (kEpi == kEpiUnpackPair) {
           y0 = reinterpret_cast<float*>(p.out) + ((b * p.chans + ch) * p.rows + r0) * C::N;
@@ -700,7 +706,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
                   const int jj = j + e * PJ;
                   const float rr = __uint_as_float(r[4 * jj + 0]), ri = __uint_as_float(r[4 * jj + 1]);
                   const float ir = __uint_as_float(r[4 * jj + 2]), ii = __uint_as_float(r[4 * jj + 3]);
-                  __half2 hh = __floats2half2_rn((rr - ii) * osc * osc2, (ir + ri) * osc * osc2);
+                  __half2 hh = __floats2half2_rn((rr - ii) * osc, (ir + ri) * osc);
                   v[e] = *reinterpret_cast<uint32_t*>(&hh);
                 }
                 // lane l of the quad stores row sl + l/2, complex pair 2 (l%2), 2 (l%2) + 1
@@ -757,8 +763,8 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
                 for (int e = 0; e < 2; ++e) {
                   const uint32_t byte = (uint32_t)(sl * C::N + kq + (int)l4 + 4 * e) * 8u;
                   float2 w = ld_shared_v2f(hbase + (byte ^ (((byte >> 7) & 7u) << 4)));
-                  w.x = w.x * osc * osc2;
-                  w.y = w.y * osc * osc2;
+                  w.x *= osc;
+                  w.y *= osc;
                   __half2 hh = __floats2half2_rn(xr[e] * w.x - xi[e] * w.y, xr[e] * w.y + xi[e] * w.x);
                   v[e] = *reinterpret_cast<uint32_t*>(&hh);
                 }
@@ -783,9 +789,12 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
             if (sig0 + sl < batch) {
               const int k = C::NS * ka + ks;
               float xr = rr - ii, xi = ir + ri;
-              if constexpr (kEpi != kEpiNatural && kEpi != kEpiMulNatural) {
+              if constexpr (kEpi == kEpiUnpackPair) {
                 xr = xr * osc * osc2;
                 xi = xi * osc * osc2;
+              } else if constexpr (kEpi != kEpiNatural && kEpi != kEpiMulNatural) {
+                xr *= osc;
+                xi *= osc;
               }
               if constexpr (kEpi == kEpiNatural) {
                 detail::store_out<kOutHalf>(p.out, (sig0 + sl) * C::N + k, xr, xi);
@@ -798,8 +807,8 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
                 } else {
                   w = __ldg(spec_t + sl * C::N + k);
                 }
-                w.x = w.x * osc * osc2;
-                w.y = w.y * osc * osc2;
+                w.x *= osc;
+                w.y *= osc;
                 detail::store_out<kOutHalf>(p.out, (sig0 + sl) * C::N + k, xr * w.x - xi * w.y, xr * w.y + xi * w.x);
               } else if constexpr (kEpi == kEpiBlocked) {
                 const int lb = p.blk_log2;
