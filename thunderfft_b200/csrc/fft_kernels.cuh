@@ -234,6 +234,26 @@ __device__ __forceinline__ int ceil_log2f(float x) {
   return e - 127 + ((b & 0x7fffffu) ? 1 : 0);
 }
 
+// Stage-2 K row of stage-2 input index r (= g2 * NA + a).  Rotated (half2):
+// row bits [2:1] = r bits [1:0], row bit 0 = r bit 2.  A half2 stage-1
+// epilogue store (4 B per lane) covers four consecutive a (one per lane of a
+// quad) at the same columns; under the 128-B swizzle (16-B chunk ^= row % 8)
+// rows that differ only in bit 0 share a 32-B chunk pair, which made every
+// such store two shared-memory wavefronts.  Rotated, the four rows land on
+// four distinct chunk pairs.  float2 (8-B stores, 32-B swizzle granules keyed
+// by row % 4, already minimal) keeps the identity.  The host permutes the
+// stage-2 DFT matrix's K columns to match.
+__host__ __device__ constexpr bool stage2_rotated(bool half, int /*n*/) { return half; }
+
+// Stage-2 column pair of stage-1 output ks (C2C kernels, NS % 8 == 0):
+// ks = 8m + 2l + h -> pair 8m + 4h + l.
+__host__ __device__ constexpr int stage2_col_pair(int ks) {
+  return (ks & ~7) | ((ks & 1) << 2) | ((ks >> 1) & 3);
+}
+__host__ __device__ constexpr int stage2_krow(bool rotated, int r) {
+  return rotated ? ((r & ~7) | ((r & 3) << 1) | ((r >> 2) & 1)) : r;
+}
+
 template <bool kHalf>
 __device__ __forceinline__ void store_complex(uint32_t saddr, float re, float im);
 template <>
@@ -282,13 +302,20 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
             const FftParams p) {
   using namespace sm100;
   using D = typename C::D;
-  // half2 C2C: the stage-2 tile is planar (re plane, im plane per signal), so a
-  // stage-2 epilogue thread holds two adjacent outputs and stores 8 bytes; a
-  // quad of lanes then writes 32 contiguous bytes (one full sector) per row.
-  // It costs the stage-1 epilogue a second (2-byte) shared store per output;
-  // measured on B200 it pays for N = 256, 1024, 2048 and not for 512, 4096.
-  constexpr bool kPlanar2 = C::kIsHalf && kEpi == kEpiNatural && kIn == kInNatural && C::NS % 8 == 0 &&
-                            (C::N == 256 || C::N == 1024 || C::N == 2048);
+  // Column pairs: the stage-1 epilogue puts output ks of stage 1 at stage-2
+  // column pair stage2_col_pair(ks) (a permutation inside each group of 8),
+  // so that the 16x256b TMEM loads of stage 2 hand a thread outputs k and
+  // k + 1 in consecutive iterations.  Each lane then stores two outputs (8 or
+  // 16 B) and a quad of lanes whole 32-B sectors, without shuffles; the
+  // stage-1 epilogue's stores keep their footprint (one aligned group of 8
+  // column pairs per row).  Used by the outputs along k: C2C, fp32 spectrum
+  // products, fp32 image rows.  Measured against plain 4/8-B stores (C2C):
+  // half2 +2 % (N = 512) to +12 % (N = 256), float2 +1-2 %, except float2
+  // N = 2048 (-5 %), which keeps plain stores; the fp32 image rows of the
+  // 2-D convolution's last pass: -24 % time (float2), -3 % (half2).
+  constexpr bool kColPairs = C::NS % 8 == 0 &&
+                             ((kEpi == kEpiNatural && kIn == kInNatural && (C::kIsHalf || C::N != 2048)) ||
+                              (kEpi == kEpiMulNatural && !(kOutHalf && C::HS > 0)) || kEpi == kEpiUnpackPair);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN];
@@ -559,20 +586,11 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
             const float2 w = tw[bi][slot];
             const int sig = g1 * C::C1 + c1;
             const int g2 = sig / C::C2, c2 = sig % C::C2;
-            const uint32_t krow = g2 * C::NA + a;
+            const uint32_t krow = (uint32_t)detail::stage2_krow(detail::stage2_rotated(C::kIsHalf, C::N), g2 * C::NA + a);
             const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
-            if constexpr (kPlanar2) {
-              // planar stage-2 columns: re plane [c2*2NS, c2*2NS + NS), im plane after it
-              const int cre = c2 * 2 * C::NS + ks, cim = cre + C::NS;
-              const uint32_t ore = (cre / C::E) * C::LBO2 + D::swz(krow * 128u + (cre % C::E) * C::ESZ);
-              const uint32_t oim = (cim / C::E) * C::LBO2 + D::swz(krow * 128u + (cim % C::E) * C::ESZ);
-              st_shared_b16(yb + ore, __half_as_ushort(__float2half_rn(zr)));
-              st_shared_b16(yb + oim, __half_as_ushort(__float2half_rn(zi)));
-            } else {
-              const int col = c2 * 2 * C::NS + 2 * ks;
-              const uint32_t off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
-              detail::store_complex<C::kIsHalf>(yb + off, zr, zi);
-            }
+            const int col = c2 * 2 * C::NS + 2 * (kColPairs ? detail::stage2_col_pair(ks) : ks);
+            const uint32_t off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
+            detail::store_complex<C::kIsHalf>(yb + off, zr, zi);
           }
         }
       }
@@ -639,40 +657,67 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
         const uint32_t cols = 256u + ((C::M2 == 64) ? 0u : (uint32_t)(buf * C::N2));
         const int rp = block * 8 + (int)(lane >> 2);
         const int g2 = rp / C::NA, ka = rp % C::NA;
-        if constexpr (kPlanar2) {
-          const bool out8 = (reinterpret_cast<uintptr_t>(p.out) & 7u) == 0;
-          // re sub-chunk jr holds ks = 8 (jr mod d) + 2l + e of its signal; the
-          // im plane of the same outputs is d = NS/8 sub-chunks later
-          constexpr int d = C::NS / 8;
-          constexpr int GC2 = (2 * C::NS > 64) ? 2 : 1;   // chunks per signal plane pair
-          static_assert(CH % GC2 == 0, "planar stage-2 chunk groups");
+        if constexpr (kColPairs) {
+          // iterations j (even) and j + 1 hold outputs k0 = NS ka + 8m + 2l
+          // and k0 + 1 of one signal (stage2_col_pair)
+          constexpr int kVec = kOutHalf ? 8 : 16;   // bytes of two complex outputs
+          const bool vec_ok = kEpi != kEpiNatural || (reinterpret_cast<uintptr_t>(p.out) & (kVec - 1)) == 0;
 #pragma unroll
-          for (int c = 0; c < CH; c += GC2) {
-            uint32_t r[GC2][32];
-#pragma unroll
-            for (int g = 0; g < GC2; ++g) tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c + g) * 64, r[g]);
+          for (int c = 0; c < CH; ++c) {
+            uint32_t r[32];
+            tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c) * 64, r);
             tmem_wait_ld();
 #pragma unroll
-            for (int g = 0; g < GC2; ++g) tmem_regs_ready(r[g]);
-#pragma unroll
-            for (int qq = 0; qq < 4 * GC2; ++qq) {
-              const int jr = (qq / d) * 2 * d + (qq % d);
-              const int col = 64 * (ch0 + c) + 8 * jr + 2 * (int)(lane & 3u);
-              const int sl = g2 * C::C2 + col / (2 * C::NS);
-              const int ks = col % (2 * C::NS);
-              uint32_t hv[2];
+            for (int j = 0; j < 8; j += 2) {
+              const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)(lane & 3u);
+              const int c2 = pidx / C::NS, pp = pidx % C::NS;     // pp = 8m + l
+              const int k0 = C::NS * ka + (pp & ~7) + 2 * (int)(lane & 3u);
+              const int sl = g2 * C::C2 + c2;
+              float xr[2], xi[2];
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const int iRR = 4 * jr + e, iIR = 4 * jr + 2 + e, iRI = 4 * (jr + d) + e, iII = 4 * (jr + d) + 2 + e;
-                const float rr = __uint_as_float(r[iRR >> 5][iRR & 31]), ir = __uint_as_float(r[iIR >> 5][iIR & 31]);
-                const float ri = __uint_as_float(r[iRI >> 5][iRI & 31]), ii = __uint_as_float(r[iII >> 5][iII & 31]);
-                __half2 hh = __floats2half2_rn(rr - ii, ir + ri);
-                hv[e] = *reinterpret_cast<uint32_t*>(&hh);
+                const int jj = j + e;
+                const float rr = __uint_as_float(r[4 * jj + 0]), ri = __uint_as_float(r[4 * jj + 1]);
+                const float ir = __uint_as_float(r[4 * jj + 2]), ii = __uint_as_float(r[4 * jj + 3]);
+                xr[e] = rr - ii;
+                xi[e] = ir + ri;
               }
               if (sig0 + sl < batch) {
-                uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + (sig0 + sl) * C::N + C::NS * ka + ks;
-                if (out8) *reinterpret_cast<uint2*>(dst) = make_uint2(hv[0], hv[1]);
-                else { dst[0] = hv[0]; dst[1] = hv[1]; }   // output only 4-byte aligned
+                if constexpr (kEpi == kEpiUnpackPair) {
+                  // fp32 real outputs: Re -> image b, Im -> image b + 1
+                  *reinterpret_cast<float2*>(y0 + sl * C::N + k0) =
+                      make_float2(xr[0] * osc * osc2, xr[1] * osc * osc2);
+                  if (y1)
+                    *reinterpret_cast<float2*>(y1 + sl * C::N + k0) =
+                        make_float2(xi[0] * osc * osc2, xi[1] * osc * osc2);
+                } else {
+                  if constexpr (kEpi == kEpiMulNatural) {
+                    // spectrum values at k0 (x, y) and k0 + 1 (z, w): one 16-B piece
+                    float4 w;
+                    if constexpr (kStageH) {
+                      const uint32_t byte = (uint32_t)(sl * C::N + k0) * 8u;
+                      w = ld_shared_v4f(hbase + (byte ^ (((byte >> 7) & 7u) << 4)));
+                    } else {
+                      w = __ldg(reinterpret_cast<const float4*>(spec_t + sl * C::N + k0));
+                    }
+                    w.x *= osc; w.y *= osc; w.z *= osc; w.w *= osc;
+                    const float a0 = xr[0] * w.x - xi[0] * w.y, b0 = xr[0] * w.y + xi[0] * w.x;
+                    const float a1 = xr[1] * w.z - xi[1] * w.w, b1 = xr[1] * w.w + xi[1] * w.z;
+                    xr[0] = a0; xi[0] = b0; xr[1] = a1; xi[1] = b1;
+                  }
+                  const long long o = (sig0 + sl) * C::N + k0;
+                  if constexpr (kOutHalf) {
+                    __half2 h0 = __floats2half2_rn(xr[0], xi[0]), h1 = __floats2half2_rn(xr[1], xi[1]);
+                    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + o;
+                    const uint32_t v0 = *reinterpret_cast<uint32_t*>(&h0), v1 = *reinterpret_cast<uint32_t*>(&h1);
+                    if (vec_ok) *reinterpret_cast<uint2*>(dst) = make_uint2(v0, v1);
+                    else { dst[0] = v0; dst[1] = v1; }   // output only 4-byte aligned
+                  } else {
+                    float2* dst = reinterpret_cast<float2*>(p.out) + o;
+                    if (vec_ok) *reinterpret_cast<float4*>(dst) = make_float4(xr[0], xi[0], xr[1], xi[1]);
+                    else { dst[0] = make_float2(xr[0], xi[0]); dst[1] = make_float2(xr[1], xi[1]); }
+                  }
+                }
               }
             }
           }
@@ -723,16 +768,13 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
               continue;
             }
           }
-          // 4-byte outputs along k (half2 spectrum products, fp32 image rows):
-          // iterations j and j + 1 hold outputs k and k + 4 of one signal, so
-          // the same quad shuffle gives each lane 8 contiguous bytes and the
-          // quad a whole 32-byte sector.  Conv-mode tiles are never partial.
-          // (Measured: it pays for the half2 spectrum products and the float2
-          // configurations' fp32 rows; the half2 configurations' fp32 rows,
-          // with one epilogue warp per lane quadrant, lose more to the
-          // shuffles than they gain.)
-          constexpr bool kPairK = ((kEpi == kEpiMulNatural && kOutHalf && kStageH) ||
-                                   (kEpi == kEpiUnpackPair && !C::kIsHalf)) && C::NS % 8 == 0;
+          // half2 spectrum products (staged spectrum): iterations j and j + 1
+          // hold outputs k and k + 4 of one signal, so a quad shuffle gives
+          // each lane 8 contiguous bytes and the quad a whole 32-byte sector.
+          // Conv-mode tiles are never partial.  (Column pairs, which need no
+          // shuffles, measured 20 % slower here: their 16-B spectrum loads
+          // from the staged tile.)
+          constexpr bool kPairK = kEpi == kEpiMulNatural && kOutHalf && kStageH && C::NS % 8 == 0;
           if constexpr (kPairK) {
             const uint32_t l4 = lane & 3u, qbase = lane & ~3u;
             const uint32_t s0 = qbase + ((2u * l4) & 3u), s1 = qbase + ((2u * l4 + 1u) & 3u);

@@ -383,6 +383,12 @@ __device__ __forceinline__ float2 ld_shared_v2f(uint32_t saddr) {
   asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(saddr) : "memory");
   return v;
 }
+__device__ __forceinline__ float4 ld_shared_v4f(uint32_t saddr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(saddr)
+               : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_shared_b16(uint32_t saddr, unsigned short v) {
   asm volatile("st.shared.b16 [%0], %1;" ::"r"(saddr), "h"(v) : "memory");
 }
