@@ -2,7 +2,9 @@
 //
 // Fragment convention of this library: with P = 32 * warp_per_block<N>
 // threads and t = threadIdx.x + 32 * threadIdx.y, thread t holds element
-// e = t + P * i (i < 32) of the block's tile in signal order (e = j*N + n).
+// e = t + P * i (i < 32) of the block's tile in signal order (e = j*N + n);
+// half2 N = 64 with 16 signals uses its MMA operand order instead
+// (frag_elem).
 // The input fragment holds input elements, the output fragment output
 // elements, both in natural order; the helpers translate to and from any
 // layout_t (strides, periodic padding, digit-reversed shared tiles).
@@ -10,6 +12,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "thunderfft_impl_device_mma.cuh"
 #include "util_arith.h"
 #include "util_cuda.h"
 
@@ -37,6 +40,21 @@ struct frag {
 };
 
 __device__ __forceinline__ int block_thread() { return threadIdx.x + threadIdx.y * blockDim.x; }
+
+// Fragment slot i of block thread t holds element n of signal j of the
+// block's tile: t + P i in signal order, except for half2 N = 64 with 16
+// signals, whose warp-MMA routine keeps the MMA operand order
+// (mfft::frag64).
+template <typename T, int N, int batch>
+__device__ __forceinline__ void frag_elem(int t, int i, int& j, int& n) {
+  if constexpr (mfft::enabled<T, N, batch>) {
+    mfft::frag64(t, i, j, n);
+  } else {
+    const int e = t + frag<N, batch>::P * i;
+    j = e / N;
+    n = e % N;
+  }
+}
 
 }  // namespace detail
 
@@ -71,8 +89,8 @@ __device__ __forceinline__ void ThunderFFT_smem2reg(vec2_t<T>* __restrict__ reg,
   const int t = detail::block_thread();
 #pragma unroll
   for (int i = 0; i < F::EPT; ++i) {
-    const int e = t + F::P * i;
-    const int j = e / sL::N, n = e % sL::N;
+    int j, n;
+    detail::frag_elem<T, sL::N, sL::batch>(t, i, j, n);
     reg[i] = smem[detail::layout_index<sL>(j, detail::stored_position<sL>(n))];
   }
 }
@@ -85,8 +103,8 @@ __device__ __forceinline__ void ThunderFFT_reg2smem(vec2_t<T>* __restrict__ smem
   const int t = detail::block_thread();
 #pragma unroll
   for (int i = 0; i < F::EPT; ++i) {
-    const int e = t + F::P * i;
-    const int j = e / sL::N, k = e % sL::N;
+    int j, k;
+    detail::frag_elem<T, sL::N, sL::batch>(t, i, j, k);
     smem[detail::layout_index<sL>(j, detail::stored_position<sL>(k))] = reg[i];
   }
 }
