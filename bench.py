@@ -166,7 +166,7 @@ def run_sweep(args):
     """Per-size table (not the contract line): every N and storage type in both
     directions at BASELINE config 3's batch 2^26/N (divided by --sweep-scale),
     plus config 3's masked partial batch (batch - 7) for half2, then the
-    conv1d (config 4) and conv2d (config 5) kernels.  Event-timed on one GPU,
+    conv1d (config 4), conv2d (config 5) and tiled conv1d kernels.  Event-timed on one GPU,
     inputs resident in HBM, each launch streaming buffers larger than L2 at
     scale 1.  Prints a markdown table."""
     import torch
@@ -224,7 +224,28 @@ def run_sweep(args):
         sweep_conv1d(args, tf, dev, g, stream, timed, peak)
     if only in ("all", "conv2d"):
         sweep_conv2d(args, tf, dev, g, stream, timed, peak)
+    if only in ("all", "tiled"):
+        sweep_tiled(args, tf, dev, g, stream, timed, peak)
     return 0
+
+
+def sweep_tiled(args, tf, dev, g, stream, timed, peak):
+    """Tiled (overlap-save) conv1d row: the reference sample's shape
+    (sample/conv1d/main.cu: one half2 sequence, 9 taps), 2^24 elements /
+    --sweep-scale.  Bandwidth counts the sequence read once and the valid
+    outputs written once."""
+    import torch
+
+    L, taps = (1 << 24) // args.sweep_scale, 9
+    x = (torch.rand(1, L, 2, device=dev, generator=g) - 0.5).half()
+    filt = torch.complex(torch.rand(taps, device=dev, generator=g) - 0.5,
+                         torch.rand(taps, device=dev, generator=g) - 0.5).contiguous()
+    op = tf.conv1d_tiled_operator(filt, "half")
+    y = torch.empty(1, L - taps + 1, 2, dtype=torch.float16, device=dev)
+    us = timed(lambda: tf.conv1d_tiled(x, op, taps, out=y, stream=stream, sync=False))
+    alg = (L + (L - taps + 1)) * 4
+    print(f"| tiled conv1d half2, {taps} taps | 64 | 1 x {L} | windows*H | {us:.1f} | {alg / us / 1e3:.0f} | "
+          f"{alg / us / 1e3 / peak:.3f} | |", flush=True)
 
 
 def sweep_conv1d(args, tf, dev, g, stream, timed, peak):
@@ -320,7 +341,7 @@ def main():
     ap.add_argument("--no-conv", action="store_true", help="sweep: skip the conv1d / conv2d rows")
     ap.add_argument("--conv-arith", default="mixed", choices=["mixed", "tf32"],
                     help="sweep: arithmetic of the conv1d / conv2d rows (default: the library default, mixed)")
-    ap.add_argument("--sweep-only", default="all", choices=["all", "fft", "conv1d", "conv2d"],
+    ap.add_argument("--sweep-only", default="all", choices=["all", "fft", "conv1d", "conv2d", "tiled"],
                     help="sweep: run only these rows (profiling one kernel)")
     args = ap.parse_args()
     configure(args.n, args.batch, args.dtype)

@@ -1140,17 +1140,29 @@ dft1_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
         tmem_ld_32x32b_x32(tmem + ((32u * q) << 16) + (uint32_t)(buf * 128 + chunk * 32), r);
         tmem_wait_ld();
         if (win_bulk) {
-          // window sig's first V outputs, contiguous after window sig-1's
+          // window sig's first V outputs, contiguous after window sig-1's.
+          // The bulk path has V * (bytes per complex) % 16 == 0 (host), so
+          // they go out as 16-byte vectors: 4 half2 or 2 float2 outputs per
+          // store.  One output per store put neighbouring lanes V * 4 bytes
+          // apart, an 8-way bank conflict for V = 56 (ncu: 3.98 M conflicts
+          // in 4.50 M store wavefronts).
+          constexpr int kPer = 16 / (2 * C::ESZ);   // outputs per 16-byte store
 #pragma unroll
-          for (int u = 0; u < 16; ++u) {
-            const int j = chunk * 16 + u;
+          for (int v = 0; v < 16 / kPer; ++v) {
+            const int j = chunk * 16 + kPer * v;
             if (j < p.win_stride) {
               const uint32_t o = (uint32_t)(sig * p.win_stride + j) * (uint32_t)(2 * C::ESZ);
               if constexpr (C::kIsHalf) {
-                __half2 t2 = __floats2half2_rn(__uint_as_float(r[2 * u]), __uint_as_float(r[2 * u + 1]));
-                st_shared_b32(sbase + o, *reinterpret_cast<uint32_t*>(&t2));
+                uint32_t h[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  __half2 t2 = __floats2half2_rn(__uint_as_float(r[2 * (4 * v + u)]),
+                                                 __uint_as_float(r[2 * (4 * v + u) + 1]));
+                  h[u] = *reinterpret_cast<uint32_t*>(&t2);
+                }
+                st_shared_v4(sbase + o, h[0], h[1], h[2], h[3]);
               } else {
-                st_shared_v2(sbase + o, __uint_as_float(r[2 * u]), __uint_as_float(r[2 * u + 1]));
+                st_shared_v4(sbase + o, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
               }
             }
           }
