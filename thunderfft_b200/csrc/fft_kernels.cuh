@@ -112,6 +112,7 @@ struct Fft2Cfg {
   using D = DType<kHalf>;
   using S = Fft2Shape<kHalf, kN, kVar>;
   static constexpr bool kIsHalf = kHalf;
+  static constexpr int kVariant = kVar;
   // kHSlots > 0 (kEpiMulNatural): the producer stages each tile's spectrum
   // rows in shared memory (kHSlots slots); the input ring shrinks to 2 tiles.
   static constexpr int HS = kHSlots;
@@ -234,24 +235,33 @@ __device__ __forceinline__ int ceil_log2f(float x) {
   return e - 127 + ((b & 0x7fffffu) ? 1 : 0);
 }
 
-// Stage-2 K row of stage-2 input index r (= g2 * NA + a).  Rotated (half2):
-// row bits [2:1] = r bits [1:0], row bit 0 = r bit 2.  A half2 stage-1
-// epilogue store (4 B per lane) covers four consecutive a (one per lane of a
-// quad) at the same columns; under the 128-B swizzle (16-B chunk ^= row % 8)
-// rows that differ only in bit 0 share a 32-B chunk pair, which made every
-// such store two shared-memory wavefronts.  Rotated, the four rows land on
-// four distinct chunk pairs.  float2 (8-B stores, 32-B swizzle granules keyed
-// by row % 4, already minimal) keeps the identity.  The host permutes the
-// stage-2 DFT matrix's K columns to match.
-__host__ __device__ constexpr bool stage2_rotated(bool half, int /*n*/) { return half; }
+// Stage-2 K row of stage-2 input index r (= g2 * NA + a): a permutation of
+// r's low three bits, chosen per configuration so that the four rows one
+// stage-1 epilogue store covers (one per lane of a quad) fall on distinct
+// shared-memory banks under the operand swizzle.  The host permutes the
+// stage-2 DFT matrix's K columns the same way.
+//   1 (half2): a store covers consecutive a; row bits [2:1] = r bits [1:0],
+//     row bit 0 = r bit 2.  Under the 128-B swizzle (16-B chunk ^= row % 8)
+//     rows differing only in bit 0 shared a 32-B chunk pair, two wavefronts
+//     per store (half2 N = 4096: 1,190,106 -> 80,228 conflicts).
+//   2 (float2, pair-planar input of the 2-D convolution's first pass): a
+//     store covers a = 8j + 2l + e, every other row; row bits [1:0] = r bits
+//     [2:1], row bit 2 = r bit 0.  The float swizzle keys its 32-B granules
+//     on row % 4, which took only two values over those rows.
+//   0: identity (float2 natural input: consecutive rows, already minimal).
+__host__ __device__ constexpr int stage2_rotation(bool half, int variant) {
+  return half ? 1 : (variant == 1 ? 2 : 0);
+}
 
 // Stage-2 column pair of stage-1 output ks (C2C kernels, NS % 8 == 0):
 // ks = 8m + 2l + h -> pair 8m + 4h + l.
 __host__ __device__ constexpr int stage2_col_pair(int ks) {
   return (ks & ~7) | ((ks & 1) << 2) | ((ks >> 1) & 3);
 }
-__host__ __device__ constexpr int stage2_krow(bool rotated, int r) {
-  return rotated ? ((r & ~7) | ((r & 3) << 1) | ((r >> 2) & 1)) : r;
+__host__ __device__ constexpr int stage2_krow(int rotation, int r) {
+  return rotation == 1   ? ((r & ~7) | ((r & 3) << 1) | ((r >> 2) & 1))
+         : rotation == 2 ? ((r & ~7) | ((r >> 1) & 3) | ((r & 1) << 2))
+                         : r;
 }
 
 template <bool kHalf>
@@ -586,7 +596,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
             const float2 w = tw[bi][slot];
             const int sig = g1 * C::C1 + c1;
             const int g2 = sig / C::C2, c2 = sig % C::C2;
-            const uint32_t krow = (uint32_t)detail::stage2_krow(detail::stage2_rotated(C::kIsHalf, C::N), g2 * C::NA + a);
+            const uint32_t krow = (uint32_t)detail::stage2_krow(detail::stage2_rotation(C::kIsHalf, C::kVariant), g2 * C::NA + a);
             const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
             const int col = c2 * 2 * C::NS + 2 * (kColPairs ? detail::stage2_col_pair(ks) : ks);
             const uint32_t off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);

@@ -108,10 +108,10 @@ size_t kmajor_noswz_off(int m, int k, int M, int esz) {
 // rows (g, ks, re|im) laid out in 16-row blocks [8 cos rows | 8 sin rows],
 // rp = g*L + ks, row = 16*(rp/8) + 8*c + rp%8; columns k = g*L + s.
 //   row (rp, 0): cos(theta), row (rp, 1): sin(theta), theta = sign*2*pi*s*ks/L
-// rotated (fft2_kernel stage 2 of the sizes thff::detail::stage2_rotated
-// names): column g*L + s sits at K index stage2_krow(true, g*L + s), the row
-// where the stage-1 epilogue puts input s of group g.
-std::vector<uint8_t> build_stage_matrix(int L, int G, int sign, bool half, bool rotated = false) {
+// rotation (fft2_kernel stage 2, thff::detail::stage2_rotation): column
+// g*L + s sits at K index stage2_krow(rotation, g*L + s), the row where the
+// stage-1 epilogue puts input s of group g.
+std::vector<uint8_t> build_stage_matrix(int L, int G, int sign, bool half, int rotation = 0) {
   const int esz = half ? 2 : 4;
   const int M = 2 * L * G, K = L * G;
   std::vector<uint8_t> img(size_t(M) * K * esz, 0);
@@ -122,7 +122,7 @@ std::vector<uint8_t> build_stage_matrix(int L, int G, int sign, bool half, bool 
         const int m = 16 * (rp / 8) + 8 * c + rp % 8;
         for (int s = 0; s < L; ++s) {
           const double th = sign * kTau * double((s * ks) % L) / double(L);
-          const int k = thff::detail::stage2_krow(rotated, g * L + s);
+          const int k = thff::detail::stage2_krow(rotation, g * L + s);
           put_value(img, kmajor_noswz_off(m, k, M, esz), c == 0 ? std::cos(th) : std::sin(th), half);
         }
       }
@@ -245,7 +245,7 @@ thff_status build_consts(int dtype, int n, bool fwd, int var, Consts* c) {
 #undef THFF_SHAPE
     if (NS == 0) return fail(THFF_INVALID_ARGUMENT, "[ThunderFFT] no such FFT shape");
     if ((st = upload(build_stage_matrix(NS, G1, sign, half), &c->a1)) != THFF_OK) return st;
-    if ((st = upload(build_stage_matrix(NA, G2, sign, half, thff::detail::stage2_rotated(half, n)), &c->a2)) !=
+    if ((st = upload(build_stage_matrix(NA, G2, sign, half, thff::detail::stage2_rotation(half, var)), &c->a2)) !=
         THFF_OK)
       return st;
   }
