@@ -29,9 +29,9 @@
 // of both in one half2 and the imaginary parts in another, so each half2
 // instruction advances two butterflies with the same twiddles.  A pass with
 // a single butterfly per thread (the radix-32 passes of N >= 1024) runs in
-// FP32 between half2 loads and stores.  half2 N = 64 (16 signals) instead
-// runs two warp-MMA DFT stages on its own fragment order
-// (thunderfft_impl_device_mma.cuh).
+// FP32 between half2 loads and stores.  half2 N = 64 (16 signals) and
+// N = 128 (8 signals) instead run two warp-MMA DFT stages on their own
+// fragment orders (thunderfft_impl_device_mma.cuh).
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -493,7 +493,8 @@ __device__ __forceinline__ void ThunderFFT_kernel_reg(vec2_t<T>* __restrict__ re
   vec2_t<T>* ws = static_cast<vec2_t<T>*>(workspace);
   const int t = detail::block_thread();
   if constexpr (detail::mfft::enabled<T, N, batch>) {
-    detail::mfft::run64<T, forward>(reg, ws, t);
+    if constexpr (N == 64) detail::mfft::run64<T, forward>(reg, ws, t);
+    else detail::mfft::run128<forward>(reg, ws, t);
   } else if constexpr (std::is_same_v<T, half>) {
     detail::dfft::run_passes_h<N, batch, F::EPT, F::P, forward, 0, 1>(reg, ws, t);
   } else {

@@ -1,5 +1,6 @@
 // thunderfft_impl_device_mma.cuh — ThunderFFT_kernel_reg for half2 N = 64 (16
-// signals, one warp) as two warp-MMA DFT stages, the form of the reference's
+// signals, one warp; and N = 128 on top of it, run128) as two warp-MMA DFT
+// stages, the form of the reference's
 // routine (detail/kernel/shared_kernel_n64_b16.cuh), written for this
 // library's own operand maps.  (The float2 branches below are kept
 // compilable and correct; see `enabled` for why float2 does not use them.)
@@ -36,6 +37,7 @@
 
 #include <cstdint>
 #include <type_traits>
+#include <utility>
 
 #include "util_arith.h"
 #include "util_cuda.h"
@@ -49,14 +51,25 @@ namespace mfft {
 // the packed-FP16 register FFT.  Its float2 form (mma.m16n8k8 .tf32, 64 MMAs
 // per call) computes correctly (rel-L2 7.5e-4) at 1.24 us, no faster than
 // the FP32 register FFT, which is also exact to 1e-7, so float2 keeps that.
+// half2 N = 128 (8 signals) reuses it on 16 rows after a radix-2 step
+// (run128).
 template <typename T, int N, int batch>
-inline constexpr bool enabled = std::is_same_v<T, half> && N == 64 && batch == 16;
+inline constexpr bool enabled =
+    std::is_same_v<T, half> && ((N == 64 && batch == 16) || (N == 128 && batch == 8));
 
 // Fragment slot i of block thread t: signal j, element n (the order above).
 __device__ __forceinline__ void frag64(int t, int i, int& j, int& n) {
   const int lane = t & 31;
   j = (lane >> 2) + 8 * (i >> 4);
   n = 16 * (lane & 3) + (i & 15);
+}
+
+// N = 128 with 8 signals: lane (gid, tig) holds signal gid, elements
+// 16 tig + i and 64 + 16 tig + i (i < 16) in slots i and 16 + i.
+__device__ __forceinline__ void frag128(int t, int i, int& j, int& n) {
+  const int lane = t & 31;
+  j = lane >> 2;
+  n = 16 * (lane & 3) + (i & 15) + 64 * (i >> 4);
 }
 
 __device__ __forceinline__ uint32_t tf32_bits(float x) {
@@ -189,14 +202,22 @@ __device__ __forceinline__ void run64(vec2_t<T>* reg, vec2_t<T>* ws, int t) {
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       V* row = ws + (gid + 8 * h) * kExSig + (4 * nt + tig) * kExRow;
+      if constexpr (kHalf) {
+        // 16-byte stores of four n_lo: with rows 68 elements apart the eight
+        // lanes of a quarter warp hit eight distinct 16-byte bank groups
+        // (8-byte stores collided up to 4-way)
 #pragma unroll
-      for (int nl = 0; nl < 8; nl += 2) {
-        const V v0 = to_vec2<T>(y[nl][nt][2 * h], y[nl][nt][2 * h + 1]);
-        const V v1 = to_vec2<T>(y[nl + 1][nt][2 * h], y[nl + 1][nt][2 * h + 1]);
-        if constexpr (kHalf) {
-          *reinterpret_cast<uint2*>(row + nl) =
-              make_uint2(*reinterpret_cast<const uint32_t*>(&v0), *reinterpret_cast<const uint32_t*>(&v1));
-        } else {
+        for (int nl = 0; nl < 8; nl += 4) {
+          uint32_t u[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) u[e] = half2_bits(y[nl + e][nt][2 * h], y[nl + e][nt][2 * h + 1]);
+          *reinterpret_cast<uint4*>(row + nl) = make_uint4(u[0], u[1], u[2], u[3]);
+        }
+      } else {
+#pragma unroll
+        for (int nl = 0; nl < 8; nl += 2) {
+          const V v0 = to_vec2<T>(y[nl][nt][2 * h], y[nl][nt][2 * h + 1]);
+          const V v1 = to_vec2<T>(y[nl + 1][nt][2 * h], y[nl + 1][nt][2 * h + 1]);
           *reinterpret_cast<float4*>(row + nl) = make_float4(v0.x, v0.y, v1.x, v1.y);
         }
       }
@@ -230,6 +251,80 @@ __device__ __forceinline__ void run64(vec2_t<T>* reg, vec2_t<T>* ws, int t) {
       reg[16 + 8 * nt + k1] = to_vec2<T>(d[2], d[3]);   // signal gid + 8
     }
   }
+}
+
+// half2 N = 128, 8 signals per warp (frag128).  A radix-2 decimation-in-
+// frequency step in registers,
+//   a[n] = x[n] + x[n + 64],  b[n] = (x[n] - x[n + 64]) w_128^n   (n < 64),
+// turns the lane's two chunks of signal gid into rows gid (a) and gid + 8 (b)
+// of the 64-point routine, whose outputs are A[k] = X[2k] and B[k] =
+// X[2k + 1].  One shared-memory pass then puts X back in frag128 order, so
+// the output order equals the input order.
+constexpr int kEx128Sig = 136;   // 8 * 136 = (128 + pad_h(128)) * 8
+__host__ __device__ constexpr int ex128_pos(int k) { return k ^ (((k >> 5) & 1) << 2); }
+
+// (cos, sin)(2 pi i / 128) for i < 16, as compile-time constants
+// (sin(x) = cos(pi/2 - x) with a short Taylor series in double).
+__host__ __device__ constexpr double taylor_cos(double x) {
+  double term = 1.0, sum = 1.0;
+  for (int k = 1; k < 12; ++k) {
+    term *= -x * x / double((2 * k - 1) * (2 * k));
+    sum += term;
+  }
+  return sum;
+}
+template <int I>
+struct Root128 {
+  static constexpr double x = 6.283185307179586476925 * I / 128.0;
+  static constexpr float c = float(taylor_cos(x)), s = float(taylor_cos(1.5707963267948966192 - x));
+};
+
+template <bool fwd, int... I>
+__device__ __forceinline__ void radix2_dif128(half2* reg, float2 wt, std::integer_sequence<int, I...>) {
+  // twiddle w_128^(16 tig + i) = w_8^tig * w_128^i: one per-lane root times a
+  // compile-time constant; applied as a packed complex multiply,
+  // (dr, di) * (wr, wi) = (dr, di) * (wr, wr) + (di, dr) * (-wi, wi)
+  (
+      [&] {
+        constexpr float ci = Root128<I>::c, si = fwd ? -Root128<I>::s : Root128<I>::s;
+        const float wr = wt.x * ci - wt.y * si, wi = wt.x * si + wt.y * ci;
+        const half2 wrr = __floats2half2_rn(wr, wr), wii = __floats2half2_rn(-wi, wi);
+        const half2 x0 = reg[I], x1 = reg[16 + I];
+        const half2 d = __hsub2(x0, x1);
+        reg[I] = __hadd2(x0, x1);
+        reg[16 + I] = __hfma2(__lowhigh2highlow(d), wii, __hmul2(d, wrr));
+      }(),
+      ...);
+}
+
+template <bool fwd>
+__device__ __forceinline__ void run128(half2* reg, half2* ws, int t) {
+  const int lane = t & 31, gid = lane >> 2, tig = lane & 3;
+  {
+    const float2 w8 = unit_root(16 * tig, 128);
+    radix2_dif128<fwd>(reg, make_float2(w8.x, fwd ? -w8.y : w8.y), std::make_integer_sequence<int, 16>{});
+  }
+  run64<half, fwd>(reg, ws, t);
+  // reg[i] = X[2k'], reg[16 + i] = X[2k' + 1], k' = 16 tig + i -> frag128
+  __syncwarp();
+  half2* row = ws + gid * kEx128Sig;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int k = 2 * (16 * tig + i);
+    *reinterpret_cast<uint2*>(row + ex128_pos(k)) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&reg[i]), *reinterpret_cast<const uint32_t*>(&reg[16 + i]));
+  }
+  __syncwarp();
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const uint4 q = *reinterpret_cast<const uint4*>(row + ex128_pos(64 * h + 16 * tig + 4 * v));
+      reg[16 * h + 4 * v + 0] = *reinterpret_cast<const half2*>(&q.x);
+      reg[16 * h + 4 * v + 1] = *reinterpret_cast<const half2*>(&q.y);
+      reg[16 * h + 4 * v + 2] = *reinterpret_cast<const half2*>(&q.z);
+      reg[16 * h + 4 * v + 3] = *reinterpret_cast<const half2*>(&q.w);
+    }
 }
 
 }  // namespace mfft

@@ -3,8 +3,8 @@
 // Fragment convention of this library: with P = 32 * warp_per_block<N>
 // threads and t = threadIdx.x + 32 * threadIdx.y, thread t holds element
 // e = t + P * i (i < 32) of the block's tile in signal order (e = j*N + n);
-// half2 N = 64 with 16 signals uses its MMA operand order instead
-// (frag_elem).
+// half2 N = 64 (16 signals) and N = 128 (8 signals) use their MMA operand
+// orders instead (frag_elem).
 // The input fragment holds input elements, the output fragment output
 // elements, both in natural order; the helpers translate to and from any
 // layout_t (strides, periodic padding, digit-reversed shared tiles).
@@ -43,12 +43,13 @@ __device__ __forceinline__ int block_thread() { return threadIdx.x + threadIdx.y
 
 // Fragment slot i of block thread t holds element n of signal j of the
 // block's tile: t + P i in signal order, except for half2 N = 64 with 16
-// signals, whose warp-MMA routine keeps the MMA operand order
-// (mfft::frag64).
+// signals and N = 128 with 8, whose warp-MMA routines keep the MMA operand
+// order (mfft::frag64, mfft::frag128).
 template <typename T, int N, int batch>
 __device__ __forceinline__ void frag_elem(int t, int i, int& j, int& n) {
   if constexpr (mfft::enabled<T, N, batch>) {
-    mfft::frag64(t, i, j, n);
+    if constexpr (N == 64) mfft::frag64(t, i, j, n);
+    else mfft::frag128(t, i, j, n);
   } else {
     const int e = t + frag<N, batch>::P * i;
     j = e / N;
