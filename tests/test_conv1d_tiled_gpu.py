@@ -25,7 +25,7 @@ def run(torch, tf, x, g, T):
 @pytest.mark.gpu
 @pytest.mark.parametrize("T", ["float", "half"])
 @pytest.mark.parametrize("L,f,batch", [(1 << 16, 9, 1), (64, 64, 1), (65, 1, 2), (1000, 33, 3),
-                                       (4097, 5, 2), (70001, 17, 1), (200, 64, 130)])
+                                       (4097, 5, 2), (70001, 17, 1), (200, 64, 130), (1 << 15, 3, 2)])
 def test_tiled_conv1d_matches_valid_correlation(cuda, T, L, f, batch):
     import torch
 
