@@ -405,6 +405,24 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
         // masked thread loads (partial last tile or unaligned input)
         const long long sig0 = tile * C::T;
         const uint32_t base = smem_u32(dst);
+        if (p.use_tma) {
+          // aligned input (the partial last tile): 16-byte vectors, 4 half2 or
+          // 2 float2 consecutive elements of one stage-1 row, which stay
+          // contiguous in the tile under either operand swizzle.  One warp
+          // loading the tile element by element kept the CTA that owns the
+          // last tile busy for microseconds after all others had finished.
+          constexpr int V = 16 / (2 * C::ESZ);
+          static_assert(C::NA % V == 0, "vectors stay inside one stage-1 row");
+#pragma unroll 4
+          for (int idx = lane; idx < C::T * C::N / V; idx += 32) {
+            const int e0 = idx * V;
+            const int sig = e0 / C::N, n = e0 % C::N;
+            const uint32_t off = detail::in_tile_offset<C>(sig, n / C::NA, n % C::NA);
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (sig0 + sig < batch) v = __ldg(reinterpret_cast<const uint4*>(p.in) + ((sig0 + sig) * C::N + n) / V);
+            st_shared_v4(base + off, v.x, v.y, v.z, v.w);
+          }
+        } else
         for (int idx = lane; idx < C::T * C::N; idx += 32) {
           const int sig = idx / C::N, n = idx % C::N;
           const int s = n / C::NA, a = n % C::NA;
