@@ -320,11 +320,11 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
   // stage-1 epilogue's stores keep their footprint (one aligned group of 8
   // column pairs per row).  Used by the outputs along k: C2C, fp32 spectrum
   // products, fp32 image rows.  Measured against plain 4/8-B stores (C2C):
-  // half2 +2 % (N = 512) to +12 % (N = 256), float2 +1-2 %, except float2
-  // N = 2048 (-5 %), which keeps plain stores; the fp32 image rows of the
-  // 2-D convolution's last pass: -24 % time (float2), -3 % (half2).
+  // half2 +2 % (N = 512) to +12 % (N = 256), float2 +1-2 % (N = 2048 within
+  // +-1 %); the fp32 image rows of the 2-D convolution's last pass: -24 %
+  // time (float2), -3 % (half2).
   constexpr bool kColPairs = C::NS % 8 == 0 &&
-                             ((kEpi == kEpiNatural && kIn == kInNatural && (C::kIsHalf || C::N != 2048)) ||
+                             ((kEpi == kEpiNatural && kIn == kInNatural) ||
                               (kEpi == kEpiMulNatural && !(kOutHalf && C::HS > 0)) || kEpi == kEpiUnpackPair);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
