@@ -231,12 +231,12 @@ def run_sweep(args):
 
 def sweep_tiled(args, tf, dev, g, stream, timed, peak):
     """Tiled (overlap-save) conv1d row: the reference sample's shape
-    (sample/conv1d/main.cu: one half2 sequence, 9 taps), 2^24 elements /
-    --sweep-scale.  Bandwidth counts the sequence read once and the valid
+    (sample/conv1d/main.cu: one half2 sequence, 9 taps by default,
+    --tiled-taps), 2^24 elements / --sweep-scale.  Bandwidth counts the sequence read once and the valid
     outputs written once."""
     import torch
 
-    L, taps = (1 << 24) // args.sweep_scale, 9
+    L, taps = (1 << 24) // args.sweep_scale, args.tiled_taps
     x = (torch.rand(1, L, 2, device=dev, generator=g) - 0.5).half()
     filt = torch.complex(torch.rand(taps, device=dev, generator=g) - 0.5,
                          torch.rand(taps, device=dev, generator=g) - 0.5).contiguous()
@@ -341,6 +341,7 @@ def main():
     ap.add_argument("--no-conv", action="store_true", help="sweep: skip the conv1d / conv2d rows")
     ap.add_argument("--conv-arith", default="mixed", choices=["mixed", "tf32"],
                     help="sweep: arithmetic of the conv1d / conv2d rows (default: the library default, mixed)")
+    ap.add_argument("--tiled-taps", type=int, default=9, help="sweep: filter taps of the tiled conv1d row (1..64)")
     ap.add_argument("--sweep-only", default="all", choices=["all", "fft", "conv1d", "conv2d", "tiled"],
                     help="sweep: run only these rows (profiling one kernel)")
     args = ap.parse_args()
