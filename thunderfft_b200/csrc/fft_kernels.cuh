@@ -85,12 +85,15 @@ struct DType<true> {
 // ---------------------------------------------------------------------------
 template <bool kHalf, int kN, int kVar = 0>
 struct Fft2Shape;
-// float2 / tf32
-template <> struct Fft2Shape<false, 128>  { static constexpr int NS = 8,  NA = 16, G1 = 4, G2 = 2, T = 32, SIN = 4, EPW = 1; };
-template <> struct Fft2Shape<false, 256>  { static constexpr int NS = 16, NA = 16, G1 = 2, G2 = 2, T = 16, SIN = 4, EPW = 1; };
-template <> struct Fft2Shape<false, 512>  { static constexpr int NS = 32, NA = 16, G1 = 1, G2 = 2, T = 8,  SIN = 4, EPW = 2; };
-template <> struct Fft2Shape<false, 1024> { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 4, EPW = 2; };
-template <> struct Fft2Shape<false, 2048> { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 3, EPW = 2; };
+// float2 / tf32.  Two input slots (SIN) for every size: measured against
+// three and four on the same box, two took N = 128 ... 2048 from 0.85-0.86
+// to 0.97-0.997 of the measured copy peak (N = 4096 already used two, at
+// 0.97).  half2 keeps eight: two lost 5-12 %, four measured the same.
+template <> struct Fft2Shape<false, 128>  { static constexpr int NS = 8,  NA = 16, G1 = 4, G2 = 2, T = 32, SIN = 2, EPW = 1; };
+template <> struct Fft2Shape<false, 256>  { static constexpr int NS = 16, NA = 16, G1 = 2, G2 = 2, T = 16, SIN = 2, EPW = 1; };
+template <> struct Fft2Shape<false, 512>  { static constexpr int NS = 32, NA = 16, G1 = 1, G2 = 2, T = 8,  SIN = 2, EPW = 2; };
+template <> struct Fft2Shape<false, 1024> { static constexpr int NS = 32, NA = 32, G1 = 1, G2 = 1, T = 4,  SIN = 2, EPW = 2; };
+template <> struct Fft2Shape<false, 2048> { static constexpr int NS = 64, NA = 32, G1 = 1, G2 = 1, T = 2,  SIN = 2, EPW = 2; };
 template <> struct Fft2Shape<false, 4096> { static constexpr int NS = 64, NA = 64, G1 = 1, G2 = 1, T = 1,  SIN = 2, EPW = 1; };
 // half2 / f16
 template <> struct Fft2Shape<true, 128>   { static constexpr int NS = 4,  NA = 32, G1 = 8, G2 = 1, T = 32, SIN = 8, EPW = 1; };
@@ -103,9 +106,9 @@ template <> struct Fft2Shape<true, 4096>  { static constexpr int NS = 64, NA = 6
 // holds 32 consecutive reals of one input row.  Used by the 2-D convolution's
 // first pass, whose pair-planar tiles keep the two real images in separate
 // 128-B column atoms.
-template <> struct Fft2Shape<false, 128, 1> { static constexpr int NS = 4,  NA = 32, G1 = 8, G2 = 1, T = 32, SIN = 4, EPW = 2; };
-template <> struct Fft2Shape<false, 256, 1> { static constexpr int NS = 8,  NA = 32, G1 = 4, G2 = 1, T = 16, SIN = 4, EPW = 2; };
-template <> struct Fft2Shape<false, 512, 1> { static constexpr int NS = 16, NA = 32, G1 = 2, G2 = 1, T = 8,  SIN = 4, EPW = 2; };
+template <> struct Fft2Shape<false, 128, 1> { static constexpr int NS = 4,  NA = 32, G1 = 8, G2 = 1, T = 32, SIN = 2, EPW = 2; };
+template <> struct Fft2Shape<false, 256, 1> { static constexpr int NS = 8,  NA = 32, G1 = 4, G2 = 1, T = 16, SIN = 2, EPW = 2; };
+template <> struct Fft2Shape<false, 512, 1> { static constexpr int NS = 16, NA = 32, G1 = 2, G2 = 1, T = 8,  SIN = 2, EPW = 2; };
 
 template <bool kHalf, int kN, int kVar = 0, int kHSlots = 0>
 struct Fft2Cfg {
