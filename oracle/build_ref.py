@@ -1,7 +1,8 @@
 """Build recipe for oracle/_ref/ — TEST INFRASTRUCTURE ONLY.
 
 Compiles, for sm_100a with nvcc directly (the reference's CMake build is not
-used), from the reference sources where they lie (/root/reference, read-only):
+used), from the reference sources where they lie (read-only; the directory is
+THFF_REFERENCE_DIR when set, else the build container's reference checkout):
   libthff_ref.so        oracle/ref_harness.cu against the reference headers
                         (its ThunderFFT_global, for parity and GPU timing);
   ref_conv1d_tiled      the reference's tiled conv1d sample as it is
@@ -18,16 +19,16 @@ Output goes only to oracle/_ref/.  Run in the build container:
 """
 from __future__ import annotations
 
+import os
 import subprocess
 import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF_INCLUDE = Path("/root/reference/include")
+REF = Path(os.environ.get("THFF_REFERENCE_DIR", "/root/reference"))
+REF_INCLUDE = REF / "include"
 OUT = HERE / "_ref" / "libthff_ref.so"
 
-
-REF = Path("/root/reference")
 SAMPLES = {
     "ref_conv1d_tiled": REF / "sample" / "conv1d" / "main.cu",
     "ref_conv1d_full": REF / "sample" / "conv1d" / "conv1d_fullfft_l4096_thunder.cu",
