@@ -210,8 +210,7 @@ thff_status thff_conv2d_set_arithmetic(int mode);
 
 /* Allocation-free variant of thff_conv2d_async (no counterpart in the
  * reference).  For callers that cannot allocate device memory where they
- * convolve: work captured into a CUDA graph (cudaMalloc breaks stream
- * capture), plugins and real-time pipelines whose host owns all device
+ * convolve: plugins and real-time pipelines whose host owns all device
  * memory, pooling allocators that must account for every byte.  The scratch
  * is a fixed 16 MiB device array inside the library (every GPU that loads
  * the library holds it until exit), so one image pair must fit in it:
@@ -219,10 +218,10 @@ thff_status thff_conv2d_set_arithmetic(int mode);
  * Any batch works (pairs are processed in passes).  The call allocates
  * nothing: call thff_initialize(THFF_F32, h) and thff_initialize(THFF_F32, w)
  * on the device beforehand.  The first call on a device resolves the array's
- * device address (cudaGetSymbolAddress); make that first call before any
- * stream capture.  Asynchronous: synchronize the stream (thff_sync_check)
- * before reading y.  All calls share the one array, so calls whose work
- * overlaps on the GPU (e.g. on two streams) race; serialize them. */
+ * device address (cudaGetSymbolAddress).  Asynchronous: synchronize the
+ * stream (thff_sync_check) before reading y.  All calls share the one
+ * array, so calls whose work overlaps on the GPU (e.g. on two streams)
+ * race; serialize them. */
 thff_status thff_conv2d_noalloc(int dtype, long long batch, int channels, int h, int w, const void* d_x,
                                 const void* d_spectra, void* d_y, void* stream);
 

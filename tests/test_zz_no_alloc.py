@@ -1,8 +1,7 @@
 """The allocation-free 2-D convolution entry point, thff_conv2d_noalloc.
 
 Callers that run the convolution where device allocation is not allowed —
-inside CUDA stream capture (cudaMalloc would invalidate the capture), inside
-plugins or real-time pipelines whose host application owns all device memory,
+inside plugins or real-time pipelines whose host application owns all device memory,
 or behind a pooling allocator that must see every byte — use this entry point
 instead of thff_conv2d, which needs a caller-allocated workspace.  Its scratch
 is a fixed 16 MiB device array inside the library.

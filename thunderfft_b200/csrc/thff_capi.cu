@@ -724,9 +724,8 @@ bool conv2d_side_ok(int v) { return v == 128 || v == 256 || v == 512 || v == 102
 // Allocation-free 2-D convolution (thff_conv2d_noalloc)
 //
 // Some callers cannot call cudaMalloc at the point where they run the
-// convolution: code recorded into a CUDA graph by stream capture (cudaMalloc
-// would break the capture), plugins and real-time pipelines whose host
-// application owns all device memory and forbids allocation on the hot path,
+// convolution: plugins and real-time pipelines whose host application owns
+// all device memory and forbids allocation on the hot path,
 // and frameworks whose pooling allocator must account for every byte.  For
 // them the scratch of the 2-D convolution lives in this fixed device array
 // instead of a caller workspace.  Every GPU that loads the library holds it
