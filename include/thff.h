@@ -38,6 +38,11 @@ const char* thff_version(void);
 /* Message of the last failing call on this thread ("" if none). */
 const char* thff_last_error(void);
 
+/* Number of kernels this library has launched in this process, on all
+ * devices (no reference counterpart).  Benchmarks and tests take the
+ * difference across a region to count the library's launches in it. */
+unsigned long long thff_launch_count(void);
+
 /* Replaces ThunderFFTInitialize<T>(N)
  * (reference: include/thunderfft/detail/thunderfft_impl_twiddle.cuh:279-327).
  * Validates N in {64,...,4096} before any CUDA call; builds/keeps one cached
@@ -71,7 +76,11 @@ thff_status thff_c2c_async(int dtype, int n, int forward, const void* d_input, v
                            long long batch, void* stream);
 
 /* Synchronizes `stream` and reports any device-side error of earlier
- * launches on this device. */
+ * launches on that stream.  Each stream has its own device error word: a
+ * bounded wait that runs out in a kernel on one stream is reported only to
+ * that stream's next thff_sync_check (which clears it) and never aborts or
+ * fails work on another stream.  A device's first 256 distinct streams get
+ * words of their own; later streams share them round robin. */
 thff_status thff_sync_check(void* stream);
 
 

@@ -242,6 +242,12 @@ int thff_oracle_circconv2d_f64(const double* x, const double* filters, const int
 //  kind 1: offset impulse (.75,.25) at (13b+7)%n
 //  kind 2: complex tone f = 1 + (7b)%(n-1), amplitude .5, phase .13b
 //  kind 3: constant (.25,-.125)
+// Kind 0 builds each element as make_float2(normal(random), normal(random))
+// (fft_validation.cu:139).  The order in which C++ evaluates two function
+// arguments is unspecified; g++ (nvcc's host compiler) evaluates them right
+// to left, so the imaginary part is drawn first.  The bit-equality of these
+// inputs with the reference's compiled generator is checked by
+// tests/test_oracle.py against tests/golden/ref_inputs.npz.
 void thff_oracle_make_validation_input(int n, int batch, int kind, float* out) {
   std::fill(out, out + size_t(2) * n * batch, 0.f);
   std::mt19937 random(1234 + n);
@@ -251,8 +257,8 @@ void thff_oracle_make_validation_input(int n, int batch, int kind, float* out) {
     if (kind == 0) {
       double sq = 0;
       for (int i = 0; i < n; ++i) {
-        const float re = normal(random);
         const float im = normal(random);
+        const float re = normal(random);
         s[2 * i] = re;
         s[2 * i + 1] = im;
         sq += double(re) * re + double(im) * im;

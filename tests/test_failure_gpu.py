@@ -73,3 +73,50 @@ def test_injected_cuda_failure_surfaces_and_library_recovers(cuda, skip):
     yd.zero_()
     tf.ThunderFFT_global("float", 1024, True, xd, yd, 16)
     assert oracle.rel_l2(yd.cpu().numpy(), oracle.fft(x)) <= 5e-3
+
+
+@pytest.mark.gpu
+def test_timeout_on_one_stream_leaves_other_streams_alone(cuda):
+    """Each stream has its own device error word.  While a bounded wait runs
+    out on stream A (3 ms bound), a queue of C2C launches runs on stream B
+    across that moment.  B's kernels must neither abort nor see A's error:
+    B's output matches the oracle and B's sync reports OK, while A alone
+    reports THFF_DEVICE_TIMEOUT.  The wait is bounded, so no GPU hangs."""
+    import threading
+    import time
+
+    import torch
+
+    import thunderfft_b200 as tf
+
+    lib = tf.load_library()
+    n, batch = 1024, 65536
+    rng = np.random.default_rng(7)
+    x = (rng.uniform(-1, 1, (batch, n)) + 1j * rng.uniform(-1, 1, (batch, n))).astype(np.complex64)
+    tf.ThunderFFTInitialize("float", n)
+    sa, sb = torch.cuda.Stream(), torch.cuda.Stream()
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty_like(xd)
+    torch.cuda.synchronize()
+    status = {}
+
+    def stall_a():
+        status["a"] = lib.thff_selftest_wait_timeout(3000, ctypes_stream(sa))
+        status["a_msg"] = lib.thff_last_error()
+
+    t = threading.Thread(target=stall_a)
+    t.start()
+    time.sleep(0.0005)
+    for _ in range(60):   # about 10 ms of transforms, straddling A's timeout
+        tf.c2c_async("float", n, True, xd, yd, batch, stream=sb)
+    tf.sync_check(sb)     # raises if B saw an error
+    t.join()
+    assert status["a"] == tf.THFF_DEVICE_TIMEOUT, status
+    assert b"timed out" in status["a_msg"]
+    sel = rng.choice(batch, 256, replace=False)
+    assert oracle.rel_l2(yd.cpu().numpy()[sel], oracle.fft(x[sel])) <= 5e-3
+    tf.sync_check(sa)     # A's word was cleared by its own read
+
+
+def ctypes_stream(stream):
+    return stream.cuda_stream

@@ -5,10 +5,16 @@
   (sample/validation/fft_validation.cu:130-163): an offset impulse is a pure
   phase ramp, a bin-aligned tone is a single bin, a constant is N*c in bin 0;
 * against the committed golden fixtures (tests/golden/make_golden.py);
+* the seeded validation inputs bit for bit against the reference's own
+  generator (digests in tests/golden/ref_inputs.json);
 * against the reference's own output: its ThunderFFT_global, recompiled for
   sm_100a and run on a B200, frozen in tests/golden/ref_gpu_outputs.npz
   (tests/golden/make_ref_gpu_golden.py).
 """
+import hashlib
+import json
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -72,11 +78,45 @@ def test_golden_fixtures_reproduced():
             x = GOLD[key.replace("_fwd", "_x")]
             assert oracle.rel_l2(oracle.fft(x, True), GOLD[key]) < 1e-13, key
     assert oracle.rel_l2(oracle.fft(GOLD["cfg1_x"], False), GOLD["cfg1_inv"]) < 1e-13
-    # generators are bit-exact restatements of the reference's
+    # the committed fixtures' inputs are the oracle's current generator output
     for n in (64, 256, 1024):
         for kind in range(4):
             assert np.array_equal(oracle.make_validation_input(n, 2, kind), GOLD[f"val_n{n}_k{kind}_x"])
     assert np.array_equal(oracle.make_fft1d_input(16), GOLD["fft1d_x"])
+
+
+REF_INPUTS = json.loads((Path(__file__).parent / "golden" / "ref_inputs.json").read_text())
+
+
+@pytest.mark.parametrize("n", SIZES)
+@pytest.mark.parametrize("kind", range(4))
+def test_validation_inputs_bit_equal_to_reference(n, kind):
+    """The oracle's restatement of the reference validation's make_input
+    (sample/validation/fft_validation.cu:130-163) reproduces the reference's
+    compiled generator bit for bit at the program's default batch: the
+    SHA-256 digests in tests/golden/ref_inputs.json come from the reference's
+    own make_input (tests/golden/make_ref_inputs.py).  Kind 0 depends on
+    g++ evaluating make_float2(normal(random), normal(random)) right to left."""
+    x = oracle.make_validation_input(n, REF_INPUTS["batch"], kind)
+    raw = np.ascontiguousarray(x.astype(np.complex64)).view(np.float32)
+    assert hashlib.sha256(raw.tobytes()).hexdigest() == REF_INPUTS["sha256"][f"n{n}_k{kind}"]
+
+
+@pytest.mark.skipif(not (oracle.HERE / "_ref" / "libthff_ref_inputs.so").exists(),
+                    reason="reference input harness not built (oracle/build_ref.py)")
+def test_validation_inputs_against_live_reference_generator():
+    """Same check against the reference's generator itself, where
+    oracle/build_ref.py has compiled it, at a batch other than the digests'."""
+    import ctypes
+
+    lib = ctypes.CDLL(str(oracle.HERE / "_ref" / "libthff_ref_inputs.so"))
+    lib.thff_ref_make_input.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    for n in SIZES:
+        for kind in range(4):
+            out = np.zeros((5, n, 2), np.float32)
+            lib.thff_ref_make_input(n, 5, kind, out.ctypes.data)
+            ref = (out[..., 0] + 1j * out[..., 1]).astype(np.complex64)
+            assert np.array_equal(oracle.make_validation_input(n, 5, kind), ref), (n, kind)
 
 
 def test_circconv1d_matches_fft_convolution():

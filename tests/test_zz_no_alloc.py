@@ -7,11 +7,17 @@ instead of thff_conv2d, which needs a caller-allocated workspace.  Its scratch
 is a fixed 16 MiB device array inside the library.
 
 This test calls the new entry point through the C ABI twice in a row, with
-different inputs, and compares each result with the existing workspace-based
-entry point on the same inputs (relative L2 <= 5e-3, the gate of the other
-tests).  It sets up everything it needs itself, so it passes in a fresh
-process as well as after the rest of the suite.  The file name makes pytest
-collect it last.
+different inputs, and checks each result three ways:
+* against the FP64 oracle's direct circular convolution (relative L2 <=
+  5e-3, the gate of the other tests);
+* against the existing workspace-based entry point running the same TF32
+  pipeline (thff_conv2d_set_arithmetic(THFF_CONV_TF32)), like for like, at a
+  tight gate;
+* that the second call leaves the device's free memory unchanged: it
+  allocates nothing.
+It sets up everything it needs itself, so it passes in a fresh process as
+well as after the rest of the suite.  The file name makes pytest collect it
+last.
 """
 import ctypes
 
@@ -21,6 +27,7 @@ import pytest
 import oracle
 
 GATE = 5e-3
+SAME_PIPELINE_GATE = 1e-5   # both entry points run the same TF32 kernels
 
 
 @pytest.mark.gpu
@@ -44,17 +51,31 @@ def test_conv2d_noalloc_matches_workspace_entry_point(cuda):
     ws = tf.conv2d_workspace(h, w, ((B + 1) // 2) * C)
     stream = torch.cuda.current_stream()
 
+    idx = np.tile(np.arange(C, dtype=np.int32), B)
     for call in range(2):
-        x = torch.from_numpy(rng.standard_normal((B, C, h, w)).astype(np.float32)).cuda()
-        expected = tf.conv2d(x, spec, ws)                       # existing entry point
+        xh = rng.standard_normal((B, C, h, w)).astype(np.float32)
+        x = torch.from_numpy(xh).cuda()
+        tf.conv2d_set_arithmetic("tf32")                         # the pipeline noalloc runs
+        try:
+            expected = tf.conv2d(x, spec, ws).cpu().numpy()      # existing entry point
+        finally:
+            tf.conv2d_set_arithmetic("mixed")                    # the library default
         y = torch.full_like(x, float("nan"))
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         st = lib.thff_conv2d_noalloc(0, B, C, h, w, x.data_ptr(), spec.data_ptr(), y.data_ptr(),
                                      stream.cuda_stream)
         assert st == tf.THFF_OK, lib.thff_last_error()
         tf.sync_check(stream)
+        free_after = torch.cuda.mem_get_info()[0]
+        if call == 1:   # a warm call: nothing may be allocated on the device
+            assert free_after == free_before, (free_before, free_after)
         got = y.cpu().numpy()
         assert np.isfinite(got).all(), call
-        assert oracle.rel_l2(got, expected.cpu().numpy()) <= GATE, call
+        assert oracle.rel_l2(got, expected) <= SAME_PIPELINE_GATE, call
+        direct = oracle.circconv2d(xh.reshape(B * C, h, w).astype(np.float64),
+                                   filt.cpu().numpy().astype(np.float64), idx).reshape(xh.shape)
+        assert oracle.rel_l2(got, direct) <= GATE, call
 
 
 def test_conv2d_noalloc_rejects_images_beyond_the_fixed_scratch():

@@ -35,7 +35,7 @@ __all__ = [
     "twiddle_table", "fft", "load_library", "library_path", "SUPPORTED_N", "batch_per_block",
     "warp_per_block", "threads_per_warp", "version", "conv1d_filter_spectrum", "conv1d",
     "conv2d_filter_spectra", "conv2d", "conv2d_workspace", "conv1d_set_arithmetic", "conv2d_set_arithmetic",
-    "conv1d_tiled_operator", "conv1d_tiled",
+    "conv1d_tiled_operator", "conv1d_tiled", "launch_count",
 ]
 
 SUPPORTED_N = (64, 128, 256, 512, 1024, 2048, 4096)
@@ -70,6 +70,8 @@ def load_library() -> ctypes.CDLL:
     vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
     lib.thff_version.restype = ctypes.c_char_p
     lib.thff_last_error.restype = ctypes.c_char_p
+    lib.thff_launch_count.argtypes = []
+    lib.thff_launch_count.restype = ctypes.c_ulonglong
     lib.thff_initialize.argtypes = [i32, i32]
     lib.thff_finalize.argtypes = [i32]
     lib.thff_twiddle_table.argtypes = [i32, ctypes.POINTER(vp), ctypes.POINTER(i32)]
@@ -192,6 +194,11 @@ def c2c_async(T, N: int, forward: bool, d_input, d_output, batch: int, stream=No
     """Asynchronous form (64-bit batch; no stream synchronization)."""
     _check(load_library().thff_c2c_async(_dtype_code(T), int(N), 1 if forward else 0, _ptr(d_input),
                                          _ptr(d_output), int(batch), _stream_handle(stream)))
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process (thff_launch_count)."""
+    return int(load_library().thff_launch_count())
 
 
 def sync_check(stream=None) -> None:

@@ -1,24 +1,30 @@
-// thff_paper_fft — the device-API timing CLI, CSV-compatible with the
-// reference's paper benchmark (sample/bench/paper_fft.cu:159-185, Table 3:
-// "differential compute time").
+// thff_paper_fft — the device-API timing CLI.  Its command line, CSV columns
+// and two stderr header lines follow the reference's paper benchmark
+// (sample/bench/paper_fft.cu:159-185, Table 3 "differential compute time"),
+// so that the two programs' outputs line up row for row:
 //
 //   thff_paper_fft N fp16|tf32 register|shared [repeats=1000] [trials=3] [batch=65536]
 //
-// One block per batch_per_block<N> signals runs the composable device API
-// (ThunderFFT_kernel_reg on a 32-element-per-thread fragment) `repeats`
-// times in a loop inside one kernel; "register" keeps the fragment in
-// registers between calls, "shared" reloads it from the block's shared tile
-// each call (smem2reg / kernel_reg / reg2smem).  compute_us =
-// (t_2R - t_R) / R cancels launch and global-memory time.  e2e_out_of_place_us
-// is one load -> FFT -> store launch.  Before timing, a 64-signal forward FFT
-// is checked against cuFFT Z2Z in FP64 on the same (rounded) input, gate
-// relative L2 <= 5e-3.  CSV columns and stderr header lines follow the
-// reference's.
+// What runs: one block per batch_per_block<N> signals calls the composable
+// device API (ThunderFFT_kernel_reg on a 32-element-per-thread fragment)
+// `repeats` times inside one kernel.  "register" keeps the fragment in
+// registers between calls; "shared" moves it through the block's shared tile
+// every call (smem2reg / kernel_reg / reg2smem).
+//   compute_us          = (t(2R) - t(R)) / R, which cancels launch and
+//                         global-memory time;
+//   e2e_out_of_place_us = one load -> FFT -> store launch.
+// Every time is the median of kRuns event-timed launches on a private stream
+// after one untimed launch of the same shape.
+// Accuracy gate (before any timing): 64 signals of the benchmark's LCG input,
+// rounded to T, through one forward FFT; relative L2 against an FP64 radix-2
+// FFT computed on the host from the same rounded values must be <= 5e-3.
 #include <thunderfft/thunderfft.cuh>
 #include <thunderfft/thunderfft_layout_tuned.h>
 #include <cufft.h>
 
+#include <algorithm>
 #include <cmath>
+#include <complex>
 #include <cstdio>
 #include <cstdlib>
 #include <stdexcept>
@@ -28,46 +34,92 @@
 
 namespace {
 
-void ck(cudaError_t e, const char* what) {
-  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
-}
-void ckf(cufftResult e, const char* what) {
-  if (e != CUFFT_SUCCESS) throw std::runtime_error(std::string(what) + ": cuFFT " + std::to_string(int(e)));
+constexpr int kRuns = 5;               // event-timed launches per figure (median)
+constexpr int kGateSignals = 64;
+constexpr double kGateLimit = 5e-3;
+
+struct CudaCall {
+  const char* what;
+  void operator<<(cudaError_t e) const {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+  }
+};
+
+struct Options {
+  int n = 0;
+  bool half = false;
+  bool shared = false;
+  int repeats = 1000;
+  int trials = 3;
+  int batch = 65536;
+};
+
+int to_int(const char* s, const char* name) {
+  char* end = nullptr;
+  const long v = std::strtol(s, &end, 10);
+  if (!end || *end || v <= 0 || v > (1L << 30)) throw std::runtime_error(std::string("invalid ") + name + ": " + s);
+  return int(v);
 }
 
-template <class T>
-__device__ vec2_t<T> enc(float x, float y) {
-  if constexpr (std::is_same_v<T, half>) return __floats2half2_rn(x, y);
-  else return make_float2(x, y);
-}
-template <class T>
-__device__ double2 widen(vec2_t<T> v) {
-  if constexpr (std::is_same_v<T, half>) return make_double2(__half2float(v.x), __half2float(v.y));
-  else return make_double2(v.x, v.y);
-}
+// ---------------------------------------------------------------- inputs
+// The accuracy input: linear-congruential values in [-1, 1) / sqrt(N) per
+// element index (re from z, im from the next step); the timed input: a real
+// sinusoid over each signal, / sqrt(N).  Both as the reference benchmark's.
+__device__ float lcg_unit(unsigned z) { return (float(int(z & 65535u)) - 32768.0f) / 32768.0f; }
 
-// Timed inputs: a real sinusoid over each signal / sqrt(N); the accuracy
-// input: linear-congruential values in [-1, 1) / sqrt(N) (both as in the
-// reference benchmark), with the FP64 copy taken after rounding to T.
 template <class T>
-__global__ void fill(vec2_t<T>* x, double2* ref, size_t count, int n) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
-    const float s = 1.0f / sqrtf((float)n);
-    float re, im;
-    if (ref) {
-      unsigned z = (unsigned)i * 1664525u + 1013904223u;
-      re = (float((int)(z & 65535u)) - 32768.0f) / 32768.0f * s;
-      z = z * 1664525u + 1013904223u;
-      im = (float((int)(z & 65535u)) - 32768.0f) / 32768.0f * s;
-    } else {
-      re = sinf(float(6.283185307179586 * double(i % n) / n)) * s;
-      im = 0.0f;
-    }
-    x[i] = enc<T>(re, im);
-    if (ref) ref[i] = widen<T>(x[i]);
+__global__ void fill_accuracy(vec2_t<T>* x, size_t count, int n) {
+  const float s = 1.0f / sqrtf(float(n));
+  const size_t step = size_t(gridDim.x) * blockDim.x;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < count; i += step) {
+    const unsigned z0 = unsigned(i) * 1664525u + 1013904223u;
+    const unsigned z1 = z0 * 1664525u + 1013904223u;
+    const float re = lcg_unit(z0) * s, im = lcg_unit(z1) * s;
+    if constexpr (std::is_same_v<T, half>) x[i] = __floats2half2_rn(re, im);
+    else x[i] = make_float2(re, im);
   }
 }
 
+template <class T>
+__global__ void fill_timing(vec2_t<T>* x, size_t count, int n) {
+  const float s = 1.0f / sqrtf(float(n));
+  const size_t step = size_t(gridDim.x) * blockDim.x;
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < count; i += step) {
+    const float re = sinf(float(6.283185307179586 * double(i % n) / n)) * s;
+    if constexpr (std::is_same_v<T, half>) x[i] = __floats2half2_rn(re, 0.0f);
+    else x[i] = make_float2(re, 0.0f);
+  }
+}
+
+template <class T>
+std::complex<double> widen(const vec2_t<T>& v) {
+  if constexpr (std::is_same_v<T, half>) return {double(__half2float(v.x)), double(__half2float(v.y))};
+  else return {double(v.x), double(v.y)};
+}
+
+// In-place FP64 radix-2 forward FFT (decimation in time, bit-reversed input
+// order), the accuracy reference.
+void fft_fp64(std::complex<double>* a, int n) {
+  for (int i = 1, j = 0; i < n; ++i) {
+    int bit = n >> 1;
+    for (; j & bit; bit >>= 1) j ^= bit;
+    j ^= bit;
+    if (i < j) std::swap(a[i], a[j]);
+  }
+  for (int len = 2; len <= n; len <<= 1) {
+    const double ang = -2.0 * M_PI / len;
+    for (int k = 0; k < len / 2; ++k) {
+      const std::complex<double> w(std::cos(ang * k), std::sin(ang * k));
+      for (int i = k; i < n; i += len) {
+        const std::complex<double> u = a[i], v = a[i + len / 2] * w;
+        a[i] = u + v;
+        a[i + len / 2] = u - v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- kernel
 template <class T, int N, bool kShared, bool kOnce>
 __global__ void bench(const vec2_t<T>* in, vec2_t<T>* out, unsigned repeats) {
   constexpr int BPB = thunderfft::batch_per_block<N>;
@@ -106,146 +158,199 @@ __global__ void bench(const vec2_t<T>* in, vec2_t<T>* out, unsigned repeats) {
   thunderfft::ThunderFFT_smem2gmem<T, L_out>(out + blockIdx.x * BPB * N, ws);
 }
 
-template <class F>
-double elapsed_us(F&& launch, int runs) {
-  cudaEvent_t a, b;
-  ck(cudaEventCreate(&a), "event");
-  ck(cudaEventCreate(&b), "event");
-  ck(cudaEventRecord(a), "record");
-  for (int i = 0; i < runs; ++i) launch();
-  ck(cudaEventRecord(b), "record");
-  ck(cudaEventSynchronize(b), "sync");
-  float ms = 0.f;
-  ck(cudaEventElapsedTime(&ms, a, b), "elapsed");
-  cudaEventDestroy(a);
-  cudaEventDestroy(b);
-  return double(ms) * 1000.0 / runs;
-}
+// ---------------------------------------------------------------- runner
+// Owns the device buffers, the stream and the events of one (T, N,
+// placement) measurement; everything is released by the destructor.
+template <class T, int N, bool kShared>
+class Runner {
+ public:
+  using V = vec2_t<T>;
+  static constexpr int BPB = thunderfft::batch_per_block<N>;
+  static constexpr int WPB = thunderfft::warp_per_block<N>;
+  static constexpr size_t kSmem = sizeof(V) * size_t(N + pad_h(N)) * BPB;
+
+  explicit Runner(const Options& o) : opt_(o) {
+    if (o.batch % BPB) throw std::runtime_error("batch must be a positive multiple of batch_per_block");
+    CudaCall{"cudaStreamCreate"} << cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking);
+    CudaCall{"cudaEventCreate"} << cudaEventCreate(&start_);
+    CudaCall{"cudaEventCreate"} << cudaEventCreate(&stop_);
+    CudaCall{"cudaFuncSetAttribute"} << cudaFuncSetAttribute(bench<T, N, kShared, false>,
+                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem));
+    CudaCall{"cudaFuncSetAttribute"} << cudaFuncSetAttribute(bench<T, N, kShared, true>,
+                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem));
+    thunderfft::ThunderFFTInitialize<T>(N);
+    initialized_ = true;
+    const size_t elems = size_t(N) * std::max(o.batch, kGateSignals);
+    CudaCall{"cudaMalloc(input)"} << cudaMalloc(&in_, elems * sizeof(V));
+    CudaCall{"cudaMalloc(output)"} << cudaMalloc(&out_, elems * sizeof(V));
+  }
+  ~Runner() {
+    if (in_) cudaFree(in_);
+    if (out_) cudaFree(out_);
+    if (start_) cudaEventDestroy(start_);
+    if (stop_) cudaEventDestroy(stop_);
+    if (stream_) cudaStreamDestroy(stream_);
+    if (initialized_) {
+      try { thunderfft::ThunderFFTFinalize<T>(); } catch (...) {}
+    }
+  }
+  Runner(const Runner&) = delete;
+  Runner& operator=(const Runner&) = delete;
+
+  // Relative L2 of one forward FFT of the accuracy input against FP64.
+  double accuracy() {
+    const size_t count = size_t(N) * kGateSignals;
+    fill_accuracy<T><<<64, 256, 0, stream_>>>(in_, count, N);
+    CudaCall{"fill"} << cudaGetLastError();
+    launch(kGateSignals, 1, true);
+    std::vector<V> x(count), y(count);
+    CudaCall{"copy input"} << cudaMemcpyAsync(x.data(), in_, count * sizeof(V), cudaMemcpyDeviceToHost, stream_);
+    CudaCall{"copy output"} << cudaMemcpyAsync(y.data(), out_, count * sizeof(V), cudaMemcpyDeviceToHost, stream_);
+    CudaCall{"synchronize"} << cudaStreamSynchronize(stream_);
+    std::vector<std::complex<double>> want(N);
+    double err = 0, ref = 0;
+    for (int s = 0; s < kGateSignals; ++s) {
+      for (int i = 0; i < N; ++i) want[i] = widen<T>(x[size_t(s) * N + i]);
+      fft_fp64(want.data(), N);
+      for (int i = 0; i < N; ++i) {
+        const std::complex<double> got = widen<T>(y[size_t(s) * N + i]);
+        if (!std::isfinite(got.real()) || !std::isfinite(got.imag())) return NAN;
+        err += std::norm(got - want[i]);
+        ref += std::norm(want[i]);
+      }
+    }
+    return std::sqrt(err / ref);
+  }
+
+  // Median event time (us) of one launch of `repeats` calls over the batch.
+  double time_us(unsigned repeats, bool once) {
+    launch(opt_.batch, repeats, once);   // untimed: same shape, warm caches
+    std::vector<double> t;
+    for (int i = 0; i < kRuns; ++i) {
+      CudaCall{"cudaEventRecord"} << cudaEventRecord(start_, stream_);
+      launch(opt_.batch, repeats, once);
+      CudaCall{"cudaEventRecord"} << cudaEventRecord(stop_, stream_);
+      CudaCall{"cudaEventSynchronize"} << cudaEventSynchronize(stop_);
+      float ms = 0.f;
+      CudaCall{"cudaEventElapsedTime"} << cudaEventElapsedTime(&ms, start_, stop_);
+      t.push_back(double(ms) * 1e3);
+    }
+    std::nth_element(t.begin(), t.begin() + kRuns / 2, t.end());
+    return t[kRuns / 2];
+  }
+
+  void prepare_timing_input() {
+    fill_timing<T><<<1024, 256, 0, stream_>>>(in_, size_t(N) * opt_.batch, N);
+    CudaCall{"fill"} << cudaGetLastError();
+    for (int w = 0; w < 3; ++w) launch(opt_.batch, unsigned(opt_.repeats), false);
+    CudaCall{"warm-up"} << cudaStreamSynchronize(stream_);
+  }
+
+ private:
+  void launch(int count, unsigned repeats, bool once) {
+    const dim3 grid(count / BPB), block(32, WPB);
+    if (once) bench<T, N, kShared, true><<<grid, block, kSmem, stream_>>>(in_, out_, repeats);
+    else bench<T, N, kShared, false><<<grid, block, kSmem, stream_>>>(in_, out_, repeats);
+    CudaCall{"bench launch"} << cudaGetLastError();
+  }
+
+  Options opt_;
+  cudaStream_t stream_ = nullptr;
+  cudaEvent_t start_ = nullptr, stop_ = nullptr;
+  V* in_ = nullptr;
+  V* out_ = nullptr;
+  bool initialized_ = false;
+};
 
 template <class T, int N, bool kShared>
-void run(int batch, int repeats, int trials) {
-  using V = vec2_t<T>;
-  constexpr int BPB = thunderfft::batch_per_block<N>;
-  constexpr int WPB = thunderfft::warp_per_block<N>;
-  constexpr size_t smem = sizeof(V) * size_t(N + pad_h(N)) * BPB;
-  if (batch <= 0 || batch % BPB) throw std::runtime_error("batch must be a positive multiple of batch_per_block");
-  ck(cudaFuncSetAttribute(bench<T, N, kShared, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "attr");
-  ck(cudaFuncSetAttribute(bench<T, N, kShared, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)), "attr");
-  thunderfft::ThunderFFTInitialize<T>(N);
-  auto launch = [&](const V* in, V* out, int count, unsigned r, bool once) {
-    const dim3 grid(count / BPB), block(32, WPB);
-    if (once) bench<T, N, kShared, true><<<grid, block, smem>>>(in, out, r);
-    else bench<T, N, kShared, false><<<grid, block, smem>>>(in, out, r);
-    ck(cudaGetLastError(), "launch");
-  };
-  // accuracy gate
-  constexpr int vb = 64;
-  const size_t vc = size_t(N) * vb;
-  V *vi = nullptr, *vo = nullptr;
-  double2* vr = nullptr;
-  ck(cudaMalloc(&vi, vc * sizeof(V)), "malloc");
-  ck(cudaMalloc(&vo, vc * sizeof(V)), "malloc");
-  ck(cudaMalloc(&vr, vc * sizeof(double2)), "malloc");
-  fill<T><<<128, 256>>>(vi, vr, vc, N);
-  ck(cudaGetLastError(), "fill");
-  cufftHandle plan;
-  ckf(cufftPlan1d(&plan, N, CUFFT_Z2Z, vb), "plan");
-  ckf(cufftExecZ2Z(plan, reinterpret_cast<cufftDoubleComplex*>(vr), reinterpret_cast<cufftDoubleComplex*>(vr),
-                   CUFFT_FORWARD), "exec");
-  launch(vi, vo, vb, 1, true);
-  ck(cudaDeviceSynchronize(), "sync");
-  std::vector<V> got(vc);
-  std::vector<double2> want(vc);
-  ck(cudaMemcpy(got.data(), vo, vc * sizeof(V), cudaMemcpyDeviceToHost), "copy");
-  ck(cudaMemcpy(want.data(), vr, vc * sizeof(double2), cudaMemcpyDeviceToHost), "copy");
-  double se = 0, sr = 0;
-  bool finite = true;
-  for (size_t i = 0; i < vc; ++i) {
-    double x, y;
-    if constexpr (std::is_same_v<T, half>) { x = __half2float(got[i].x); y = __half2float(got[i].y); }
-    else { x = got[i].x; y = got[i].y; }
-    finite = finite && std::isfinite(x) && std::isfinite(y);
-    se += (x - want[i].x) * (x - want[i].x) + (y - want[i].y) * (y - want[i].y);
-    sr += want[i].x * want[i].x + want[i].y * want[i].y;
-  }
-  const double rel = std::sqrt(se / sr);
-  cufftDestroy(plan);
-  cudaFree(vi); cudaFree(vo); cudaFree(vr);
-  if (!finite || !(rel <= 5e-3)) throw std::runtime_error("single-FFT correctness gate failed relL2=" + std::to_string(rel));
-  // timing
-  V *in = nullptr, *out = nullptr;
-  const size_t bytes = size_t(N) * batch * sizeof(V);
-  ck(cudaMalloc(&in, bytes), "malloc");
-  ck(cudaMalloc(&out, bytes), "malloc");
-  fill<T><<<1024, 256>>>(in, nullptr, size_t(N) * batch, N);
-  ck(cudaDeviceSynchronize(), "fill");
-  for (int w = 0; w < 3; ++w) { launch(in, out, batch, unsigned(repeats), false); ck(cudaDeviceSynchronize(), "warmup"); }
-  for (int t = 0; t < trials; ++t) {
-    launch(in, out, batch, unsigned(repeats), false);
-    ck(cudaDeviceSynchronize(), "sync");
-    const double t_r = elapsed_us([&] { launch(in, out, batch, unsigned(repeats), false); }, 1);
-    launch(in, out, batch, unsigned(2 * repeats), false);
-    ck(cudaDeviceSynchronize(), "sync");
-    const double t_2r = elapsed_us([&] { launch(in, out, batch, unsigned(2 * repeats), false); }, 1);
+void measure(const Options& o) {
+  Runner<T, N, kShared> run(o);
+  const double rel = run.accuracy();
+  if (!(rel <= kGateLimit)) throw std::runtime_error("accuracy gate failed: relative L2 " + std::to_string(rel));
+  run.prepare_timing_input();
+  const unsigned r = unsigned(o.repeats);
+  for (int trial = 0; trial < o.trials; ++trial) {
+    const double t_r = run.time_us(r, false);
+    const double t_2r = run.time_us(2 * r, false);
     if (!(std::isfinite(t_r) && std::isfinite(t_2r) && t_2r > t_r))
-      throw std::runtime_error("nonpositive/nonfinite differential timing");
-    launch(in, out, batch, 1, true);
-    ck(cudaDeviceSynchronize(), "sync");
-    const double e2e = elapsed_us([&] { launch(in, out, batch, 1, true); }, 10);
-    std::printf("%d,%s,%s,%d,%d,%d,%.9g,%.9g,%.9g,%.9g,%.12g,%zu\n", N, std::is_same_v<T, half> ? "fp16" : "tf32",
-                kShared ? "shared" : "register", batch, repeats, t, t_r, t_2r, (t_2r - t_r) / repeats, e2e, rel, smem);
+      throw std::runtime_error("differential timing is not positive");
+    const double e2e = run.time_us(1, true);
+    std::printf("%d,%s,%s,%d,%d,%d,%.9g,%.9g,%.9g,%.9g,%.12g,%zu\n", N, o.half ? "fp16" : "tf32",
+                o.shared ? "shared" : "register", o.batch, o.repeats, trial, t_r, t_2r, (t_2r - t_r) / r, e2e, rel,
+                Runner<T, N, kShared>::kSmem);
     std::fflush(stdout);
   }
-  cudaFree(in);
-  cudaFree(out);
-  thunderfft::ThunderFFTFinalize<T>();
 }
 
+// Every (N, type, placement) the CLI accepts, as one table.
+struct Entry {
+  int n;
+  bool half, shared;
+  void (*fn)(const Options&);
+};
 template <int N>
-void choose(const std::string& prec, const std::string& place, int b, int r, int t) {
-  if (prec == "fp16") {
-    if (place == "shared") run<half, N, true>(b, r, t); else run<half, N, false>(b, r, t);
-  } else {
-    if (place == "shared") run<float, N, true>(b, r, t); else run<float, N, false>(b, r, t);
+constexpr Entry entries_for(int which) {
+  return which == 0   ? Entry{N, false, false, &measure<float, N, false>}
+         : which == 1 ? Entry{N, false, true, &measure<float, N, true>}
+         : which == 2 ? Entry{N, true, false, &measure<half, N, false>}
+                      : Entry{N, true, true, &measure<half, N, true>};
+}
+template <int... Ns>
+struct Table {
+  static constexpr int kCount = 4 * int(sizeof...(Ns));
+  Entry e[kCount];
+  constexpr Table() : e{} {
+    int i = 0;
+    ((e[i++] = entries_for<Ns>(0), e[i++] = entries_for<Ns>(1), e[i++] = entries_for<Ns>(2),
+      e[i++] = entries_for<Ns>(3)), ...);
   }
+};
+constexpr Table<64, 128, 256, 512, 1024, 2048, 4096> kTable;
+
+Options parse(int argc, char** argv) {
+  Options o;
+  o.n = to_int(argv[1], "N");
+  const std::string prec = argv[2], place = argv[3];
+  if (prec != "fp16" && prec != "tf32") throw std::runtime_error("precision must be fp16 or tf32");
+  if (place != "register" && place != "shared") throw std::runtime_error("placement must be register or shared");
+  o.half = prec == "fp16";
+  o.shared = place == "shared";
+  if (argc > 4) o.repeats = to_int(argv[4], "repeats");
+  if (argc > 5) o.trials = to_int(argv[5], "trials");
+  if (argc > 6) o.batch = to_int(argv[6], "batch");
+  return o;
+}
+
+void print_headers(const Options& o) {
+  cudaDeviceProp prop;
+  CudaCall{"cudaGetDeviceProperties"} << cudaGetDeviceProperties(&prop, 0);
+  int driver = 0, runtime = 0, cufft = 0;
+  CudaCall{"cudaDriverGetVersion"} << cudaDriverGetVersion(&driver);
+  CudaCall{"cudaRuntimeGetVersion"} << cudaRuntimeGetVersion(&runtime);
+  if (cufftGetVersion(&cufft) != CUFFT_SUCCESS) cufft = 0;
+  std::fprintf(stderr, "compiled_CUDART=%d runtime=%d driver=%d cuFFT=%d extra_R_warmups=3\n", CUDART_VERSION, runtime,
+               driver, cufft);
+  std::fprintf(stderr, "GPU=%s compute=%d.%d batch=%d R=%d trials=%d single_fft_relL2_limit=0.005\n", prop.name,
+               prop.major, prop.minor, o.batch, o.repeats, o.trials);
+  std::puts("N,precision,placement,batch,inside_repeats,trial,t_R_us,t_2R_us,compute_us,e2e_out_of_place_us,"
+            "single_fft_relL2,shared_bytes");
 }
 
 }  // namespace
 
 int main(int argc, char** argv) {
+  if (argc < 4 || argc > 7) {
+    std::fprintf(stderr, "usage: %s N fp16|tf32 register|shared [repeats=1000] [trials=3] [batch=65536]\n", argv[0]);
+    return 2;
+  }
   try {
-    if (argc < 4 || argc > 7) {
-      std::fprintf(stderr, "usage: %s N fp16|tf32 register|shared [repeats=1000] [trials=3] [batch=65536]\n", argv[0]);
-      return 2;
-    }
-    const int n = std::stoi(argv[1]);
-    const int r = argc > 4 ? std::stoi(argv[4]) : 1000, t = argc > 5 ? std::stoi(argv[5]) : 3;
-    const int b = argc > 6 ? std::stoi(argv[6]) : 65536;
-    const std::string prec = argv[2], place = argv[3];
-    if ((prec != "fp16" && prec != "tf32") || (place != "register" && place != "shared") || r <= 0 || t <= 0)
-      throw std::runtime_error("invalid arguments");
-    cudaDeviceProp prop;
-    ck(cudaGetDeviceProperties(&prop, 0), "properties");
-    int drv = 0, rt = 0, cufft_v = 0;
-    cudaDriverGetVersion(&drv);
-    cudaRuntimeGetVersion(&rt);
-    cufftGetVersion(&cufft_v);
-    std::fprintf(stderr, "compiled_CUDART=%d runtime=%d driver=%d cuFFT=%d extra_R_warmups=3\n", CUDART_VERSION, rt,
-                 drv, cufft_v);
-    std::fprintf(stderr, "GPU=%s compute=%d.%d batch=%d R=%d trials=%d single_fft_relL2_limit=0.005\n", prop.name,
-                 prop.major, prop.minor, b, r, t);
-    std::puts("N,precision,placement,batch,inside_repeats,trial,t_R_us,t_2R_us,compute_us,e2e_out_of_place_us,"
-              "single_fft_relL2,shared_bytes");
-    switch (n) {
-      case 64: choose<64>(prec, place, b, r, t); break;
-      case 128: choose<128>(prec, place, b, r, t); break;
-      case 256: choose<256>(prec, place, b, r, t); break;
-      case 512: choose<512>(prec, place, b, r, t); break;
-      case 1024: choose<1024>(prec, place, b, r, t); break;
-      case 2048: choose<2048>(prec, place, b, r, t); break;
-      case 4096: choose<4096>(prec, place, b, r, t); break;
-      default: throw std::runtime_error("unsupported N");
-    }
+    const Options o = parse(argc, argv);
+    const Entry* hit = nullptr;
+    for (const Entry& e : kTable.e)
+      if (e.n == o.n && e.half == o.half && e.shared == o.shared) hit = &e;
+    if (!hit) throw std::runtime_error("unsupported N: " + std::to_string(o.n));
+    print_headers(o);
+    hit->fn(o);
     return 0;
   } catch (const std::exception& e) {
     std::fprintf(stderr, "ERROR: %s\n", e.what());

@@ -60,6 +60,15 @@ cudaError_t injected(cudaError_t real) {
   return e;
 }
 
+// Kernels this library has launched in this process (all devices); every
+// launch site checks its launch through launched().
+std::atomic<unsigned long long> g_launches{0};
+
+cudaError_t launched() {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
 #define THFF_CUDA(expr, what)                      \
   do {                                             \
     cudaError_t e_ = injected(expr);               \
@@ -163,18 +172,45 @@ struct RefCache {          // reference-compatible twiddle cache entry
   int n = 0;
 };
 
+// Device error words, one per stream.  A kernel's bounded wait that runs
+// out records its code in the word of the stream it was launched on, and
+// every wait of that launch gives up once the word is non-zero, so a stalled
+// CTA drains instead of waiting for work that will not come.  Launches on
+// other streams have their own words: a timeout on one stream neither aborts
+// another stream's kernels nor is reported to that stream's caller.  A word
+// stays set until thff_sync_check on its stream reads it; the read clears it
+// in stream order.  The words live in this fixed device array (no
+// allocation); a device's first kErrSlots distinct streams get words of
+// their own, later streams share them round robin.
+constexpr int kErrSlots = 256;
+static __device__ uint32_t g_err_words[kErrSlots];
+
 struct DeviceState {
   bool ready = false;
   int sms = 0;
-  uint32_t* d_err = nullptr;
+  uint32_t* d_err_words = nullptr;           // device address of g_err_words
+  std::map<cudaStream_t, int> err_slot;      // stream -> index into g_err_words
+  int err_next = 0;
   std::map<int, Consts> consts;  // key = (dtype*2 + fwd)*8192 + N
   RefCache ref[2];
   std::map<const void*, bool> attr_done;
 };
 
 std::mutex g_mutex;
+std::mutex g_err_mutex;                      // guards DeviceState::err_slot / err_next
 std::map<int, DeviceState> g_dev;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+// The error word of `stream` on this device.
+uint32_t* stream_err(DeviceState& st, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(g_err_mutex);
+  auto it = st.err_slot.find(stream);
+  if (it == st.err_slot.end()) {
+    it = st.err_slot.emplace(stream, st.err_next).first;
+    st.err_next = (st.err_next + 1) % kErrSlots;
+  }
+  return st.d_err_words + it->second;
+}
 
 thread_local uint32_t* t_err_host = nullptr;  // pinned readback word per thread
 
@@ -192,8 +228,9 @@ thff_status ensure_device(int dev, DeviceState** out) {
       return fail(THFF_UNSUPPORTED, std::string("[ThunderFFT] this build targets sm_100a (B200); device is ") +
                                         prop.name + " sm_" + std::to_string(prop.major) + std::to_string(prop.minor));
     st.sms = prop.multiProcessorCount;
-    THFF_CUDA(cudaMalloc(&st.d_err, sizeof(uint32_t)), "cudaMalloc(error word)");
-    THFF_CUDA(cudaMemset(st.d_err, 0, sizeof(uint32_t)), "cudaMemset(error word)");
+    THFF_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&st.d_err_words), g_err_words),
+              "cudaGetSymbolAddress(error words)");
+    THFF_CUDA(cudaMemset(st.d_err_words, 0, sizeof(uint32_t) * kErrSlots), "cudaMemset(error words)");
     if (!g_encode) {
       cudaDriverEntryPointQueryResult q;
       void* fn = nullptr;
@@ -389,7 +426,7 @@ thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* 
   std::memset(&p, 0, sizeof(p));
   if (extra) p = *extra;
   p.in = in; p.out = out; p.a1 = c.a1; p.a2 = c.a2; p.tw = reinterpret_cast<const float2*>(c.tw);
-  p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = st.d_err;
+  p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = stream_err(st, stream);
   if (!extra) { p.rows = 1; p.chans = 1; p.ppc = 1; }
   // spectrum staging (kEpiMulNatural with slots): the spectra as 128-B lines,
   // one box = the T*N complex values of one tile
@@ -411,7 +448,7 @@ thff_status launch_fft2(DeviceState& st, const Consts& c, const void* in, void* 
   if (s != THFF_OK) return s;
   const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
   kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map, map_spec, p);
-  THFF_CUDA(cudaGetLastError(), "ThunderFFT_global launch");
+  THFF_CUDA(launched(), "ThunderFFT_global launch");
   return THFF_OK;
 }
 
@@ -437,12 +474,12 @@ thff_status launch_dft1(DeviceState& st, const Consts& c, const void* in, void* 
     return s;
   thff::FftParams p;
   p.in = in; p.out = out; p.a1 = c.a1; p.a2 = nullptr; p.tw = nullptr;
-  p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = st.d_err;
+  p.batch = batch; p.use_tma = use_tma ? 1 : 0; p.err = stream_err(st, stream);
   auto kernel = thff::dft1_kernel<C>;
   if ((s = set_smem_attr(st, kernel, int(C::SMEM_BYTES))) != THFF_OK) return s;
   const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
   kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map_in, map_out, p, tma_store ? 1 : 0);
-  THFF_CUDA(cudaGetLastError(), "ThunderFFT_global launch");
+  THFF_CUDA(launched(), "ThunderFFT_global launch");
   return THFF_OK;
 }
 
@@ -476,14 +513,14 @@ thff_status launch_conv1d_tiled(DeviceState& st, const void* op, const void* in,
                     strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) != THFF_OK)
       return s;
   }
-  p.in = in; p.out = out; p.a1 = op; p.batch = windows; p.use_tma = tma_in ? 1 : 0; p.err = st.d_err;
+  p.in = in; p.out = out; p.a1 = op; p.batch = windows; p.use_tma = tma_in ? 1 : 0; p.err = stream_err(st, stream);
   p.win_stride = int(stride); p.win_per_sig = wps; p.in_len = in_len; p.out_len = out_len;
   p.win_tmax = in_len >= C::N ? (in_len - C::N) / stride : -1;
   auto kernel = thff::dft1_kernel<C, true>;
   if ((s = set_smem_attr(st, kernel, int(C::SMEM_BYTES))) != THFF_OK) return s;
   const long long grid = num_tiles < st.sms ? num_tiles : st.sms;
   kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map_in, map_out, p, bulk_out ? 1 : 0);
-  THFF_CUDA(cudaGetLastError(), "tiled conv1d launch");
+  THFF_CUDA(launched(), "tiled conv1d launch");
   return THFF_OK;
 }
 
@@ -525,13 +562,13 @@ thff_status launch_conv1d(DeviceState& st, const Consts& c, int lin, const void*
   p.batch = batch;
   p.lin = lin;
   p.rows_valid = lin / C::L;
-  p.err = st.d_err;
+  p.err = stream_err(st, stream);
   auto kernel = thff::conv1d_kernel<C>;
   if ((s = set_smem_attr(st, kernel, int(C::SMEM_BYTES))) != THFF_OK) return s;
   const long long tiles = (batch + 2 * C::TC - 1) / (2 * C::TC);
   const long long grid = tiles < st.sms ? tiles : st.sms;
   kernel<<<unsigned(grid), C::kThreads, C::SMEM_BYTES, stream>>>(map, p);
-  THFF_CUDA(cudaGetLastError(), "conv1d launch");
+  THFF_CUDA(launched(), "conv1d launch");
   return THFF_OK;
 }
 
@@ -681,9 +718,9 @@ thff_status conv2d_run_h(DeviceState& st, LookupF&& consts_f, LookupH&& consts_h
   THFF_CUDA(cudaMemsetAsync(amax, 0, sizeof(unsigned), cs), "conv2d range word");
   thff::conv2d_spectra_absmax_kernel<<<unsigned(4 * st.sms), 256, 0, cs>>>(static_cast<const float*>(d_spectra),
                                                                           2LL * chans * h * w, amax);
-  THFF_CUDA(cudaGetLastError(), "conv2d range launch");
+  THFF_CUDA(launched(), "conv2d range launch");
   thff::conv2d_call_exp_kernel<<<1, 1, 0, cs>>>(amax, h, e);
-  THFF_CUDA(cudaGetLastError(), "conv2d range launch");
+  THFF_CUDA(launched(), "conv2d range launch");
   thff::FftParams ex;
   std::memset(&ex, 0, sizeof(ex));
   ex.chans = chans; ex.nimg_b = nimg_b; ex.ppc = ppc; ex.spec = static_cast<const float2*>(d_spectra);
@@ -693,7 +730,7 @@ thff_status conv2d_run_h(DeviceState& st, LookupF&& consts_f, LookupH&& consts_h
     ex.pair0 = p0;
     thff::conv2d_pair_exp_kernel<<<unsigned(np), 256, 0, cs>>>(static_cast<const float*>(d_x), nimg_b, chans, ppc,
                                                                 p0, h, w, e + 2);
-    THFF_CUDA(cudaGetLastError(), "conv2d range launch");
+    THFF_CUDA(launched(), "conv2d range launch");
     ex.rows = h;                     // P1: h row signals per image
     ex.blk_log2 = ilog2(conv2d_c1(h, true));
     ex.conv_pass = 1;
@@ -731,9 +768,10 @@ bool conv2d_side_ok(int v) { return v == 128 || v == 256 || v == 512 || v == 102
 // instead of a caller workspace.  Every GPU that loads the library holds it
 // (kNoAllocScratchBytes) until the process exits.
 // ---------------------------------------------------------------------------
-constexpr long long kNoAllocScratchBytes = 16LL << 20;  // 16 MiB: one pass holds scratch/(2*h*w*16) image pairs
+// 16 MiB: one pass holds scratch / per_pair image pairs, per_pair = 2*h*w*8
+// bytes (the two float2 scratch images z0, z1 of one pair).
+constexpr long long kNoAllocScratchBytes = 16LL << 20;
 static __device__ __align__(256) unsigned char g_conv2d_scratch[kNoAllocScratchBytes];
-std::map<int, void*> g_noalloc_scratch;  // device -> address of g_conv2d_scratch (under g_mutex)
 
 // Look up FFT constants without building them (building would allocate).
 const Consts* find_consts(DeviceState& st, int dtype, int n, bool fwd, int var = 0) {
@@ -741,15 +779,18 @@ const Consts* find_consts(DeviceState& st, int dtype, int n, bool fwd, int var =
   return it == st.consts.end() ? nullptr : &it->second;
 }
 
+// Synchronizes `stream` and reads (and clears) its error word.  Another
+// stream's word is never touched.
 thff_status read_device_error(DeviceState& st, cudaStream_t stream) {
   if (!t_err_host) THFF_CUDA(cudaMallocHost(&t_err_host, sizeof(uint32_t)), "cudaMallocHost(error word)");
   *t_err_host = 0;
-  THFF_CUDA(cudaMemcpyAsync(t_err_host, st.d_err, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
+  uint32_t* word = stream_err(st, stream);
+  THFF_CUDA(cudaMemcpyAsync(t_err_host, word, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream),
             "cudaMemcpyAsync(error word)");
   THFF_CUDA(cudaStreamSynchronize(stream), "ThunderFFT_global synchronize");
   if (*t_err_host != 0) {
     const uint32_t code = *t_err_host;
-    cudaMemsetAsync(st.d_err, 0, sizeof(uint32_t), stream);
+    cudaMemsetAsync(word, 0, sizeof(uint32_t), stream);
     cudaStreamSynchronize(stream);
     return fail(THFF_DEVICE_TIMEOUT, "[ThunderFFT] device pipeline wait timed out (code " + std::to_string(code) + ")");
   }
@@ -763,6 +804,8 @@ extern "C" {
 const char* thff_version(void) { return "thunderfft_b200 0.1 (sm_100a tcgen05/TMA)"; }
 
 const char* thff_last_error(void) { return g_last_error.c_str(); }
+
+unsigned long long thff_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 thff_status thff_initialize(int dtype, int n) {
   if (!valid_dtype(dtype)) return fail(THFF_INVALID_ARGUMENT, "ThunderFFTInitialize<T>: supported T are float and half only");
@@ -896,8 +939,8 @@ thff_status thff_selftest_wait_timeout(int limit_us, void* stream) {
     if ((s = ensure_device(dev, &st)) != THFF_OK) return s;
   }
   cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-  thff::wait_timeout_selftest_kernel<<<1, 32, 0, cs>>>(st->d_err, 1000ull * (unsigned long long)limit_us);
-  THFF_CUDA(cudaGetLastError(), "selftest launch");
+  thff::wait_timeout_selftest_kernel<<<1, 32, 0, cs>>>(stream_err(*st, cs), 1000ull * (unsigned long long)limit_us);
+  THFF_CUDA(launched(), "selftest launch");
   return read_device_error(*st, cs);
 }
 
@@ -921,7 +964,7 @@ thff_status thff_conv1d_filter_spectrum(int dtype, int n, const float* d_filter,
   if (!d_filter || !d_spectrum) return fail(THFF_INVALID_ARGUMENT, "conv1d: null filter or spectrum");
   thff::conv1d_spectrum_kernel<<<(n + 255) / 256, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       d_filter, taps, n, static_cast<float2*>(d_spectrum));
-  THFF_CUDA(cudaGetLastError(), "conv1d spectrum launch");
+  THFF_CUDA(launched(), "conv1d spectrum launch");
   return THFF_OK;
 }
 
@@ -982,7 +1025,7 @@ thff_status thff_conv1d_tiled_operator(int dtype, const void* d_filter, int f, v
   else
     thff::conv1d_tiled_operator_kernel<false><<<(total + 255) / 256, 256, 0, cs>>>(
         static_cast<const float2*>(d_filter), f, static_cast<uint8_t*>(d_operator));
-  THFF_CUDA(cudaGetLastError(), "tiled conv1d operator launch");
+  THFF_CUDA(launched(), "tiled conv1d operator launch");
   return THFF_OK;
 }
 
@@ -1056,9 +1099,9 @@ thff_status thff_conv2d_filter_spectra(int dtype, int h, int w, int chans, int f
   double2* g = static_cast<double2*>(d_workspace);
   const long long n1 = (long long)chans * f * w, n2 = (long long)chans * h * w;
   thff::conv2d_filter_rows_kernel<<<unsigned((n1 + 255) / 256), 256, 0, cs>>>(d_filters, chans, f, w, g);
-  THFF_CUDA(cudaGetLastError(), "conv2d filter spectrum launch");
+  THFF_CUDA(launched(), "conv2d filter spectrum launch");
   thff::conv2d_filter_cols_kernel<<<unsigned((n2 + 255) / 256), 256, 0, cs>>>(g, chans, f, h, w, static_cast<float2*>(d_spectra));
-  THFF_CUDA(cudaGetLastError(), "conv2d filter spectrum launch");
+  THFF_CUDA(launched(), "conv2d filter spectrum launch");
   return THFF_OK;
 }
 
@@ -1143,15 +1186,12 @@ thff_status thff_conv2d_noalloc(int dtype, long long nimg_b, int chans, int h, i
       return fail(THFF_INVALID_ARGUMENT, "thff_conv2d_noalloc: call thff_initialize on this device first "
                                          "(this entry point allocates nothing)");
     st = &it->second;
-    auto sc = g_noalloc_scratch.find(dev);
-    if (sc == g_noalloc_scratch.end()) {
-      // first call on this device: resolve the device address of the array
-      void* ptr = nullptr;
-      THFF_CUDA(cudaGetSymbolAddress(&ptr, g_conv2d_scratch), "cudaGetSymbolAddress(conv2d scratch)");
-      sc = g_noalloc_scratch.emplace(dev, ptr).first;
-    }
-    scratch = sc->second;
   }
+  // The device address of the array in the current device's context.  It is
+  // looked up on every call (the lookup allocates nothing), so an address
+  // never outlives the context it belongs to.  In host code the array's name
+  // is only a host-side stand-in and must not be passed to a kernel.
+  THFF_CUDA(cudaGetSymbolAddress(&scratch, g_conv2d_scratch), "cudaGetSymbolAddress(conv2d scratch)");
   const long long chunk = kNoAllocScratchBytes / per_pair;
   float2* z0 = static_cast<float2*>(scratch);
   float2* z1 = z0 + (size_t)chunk * h * w;
