@@ -101,6 +101,7 @@ class ClockSampler:
         self.cuda_index = cuda_index
         self.period = period_s
         self.samples = []
+        self.extra = []          # (memory MHz, power W, GPU temperature C) per sample
         self.max_mhz = None
         self.error = None
         self._stop = threading.Event()
@@ -142,10 +143,14 @@ class ClockSampler:
         return int(f(self._h))
 
     def _run(self):
+        nv = self._nvml
         while not self._stop.is_set():
             try:
-                mhz = float(self._nvml.nvmlDeviceGetClockInfo(self._h, self._nvml.NVML_CLOCK_SM))
+                mhz = float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
                 self.samples.append((mhz, self._reasons()))
+                self.extra.append((float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_MEM)),
+                                   float(nv.nvmlDeviceGetPowerUsage(self._h)) / 1000.0,
+                                   float(nv.nvmlDeviceGetTemperature(self._h, nv.NVML_TEMPERATURE_GPU))))
             except Exception as e:
                 self.error = f"{type(e).__name__}: {e}"
                 return
@@ -165,8 +170,14 @@ class ClockSampler:
             for bit, name in self.REASONS.items():
                 if r & bit:
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml, 10 ms, timed region"}
+        out = {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml, 10 ms, timed region"}
+        if self.extra:
+            out["mem_mhz"] = statistics.median(e[0] for e in self.extra)
+            out["power_w_median"] = statistics.median(e[1] for e in self.extra)
+            out["power_w_max"] = max(e[1] for e in self.extra)
+            out["temp_c_first_last"] = [self.extra[0][2], self.extra[-1][2]]
+        return out
 
 
 class CuFFT:
@@ -678,6 +689,7 @@ def run_c2c(args):
             "gpu_launches": launches,
             "timing": {"repeats": len(reps), "steps_per_repeat": args.steps,
                        "ms_min": min(reps), "ms_median": ms_max, "ms_max": max(reps),
+                       "ms_each": [round(v, 4) for v in reps],
                        "how": "each repeat: barrier + sync, K steps event-timed on the launch stream, sync + "
                               "barrier; max over ranks per repeat; median over repeats"},
             "clocks": clocks,
@@ -837,7 +849,8 @@ def run_conv2d(args):
             "e2e": e2e,
             "gpu_launches": launches,
             "timing": {"repeats": len(reps), "steps_per_repeat": args.steps,
-                       "ms_min": min(reps), "ms_median": ms_max, "ms_max": max(reps)},
+                       "ms_min": min(reps), "ms_median": ms_max, "ms_max": max(reps),
+                       "ms_each": [round(v, 4) for v in reps]},
             "clocks": clocks,
             "gate_rel_l2": gate_err,
         }

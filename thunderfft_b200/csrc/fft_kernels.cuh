@@ -186,6 +186,9 @@ struct FftParams {
   // outputs by 2^e, e = conv_pass 1: e1, 2: e2, 3: e3, 4: -(e1 + e2 + e3).
   const int* conv_exp;
   int conv_pass;
+  // Fused conv2d column pass (conv2d_cols_kernel): A image of the inverse's
+  // second stage (A1 with stage 2's K-row rotation).
+  const void* a4;
   // Overlapping windows (dft1_kernel<C, true>, the tiled convolution): signal
   // w is window t = w % win_per_sig of sequence b = w / win_per_sig, i.e.
   // in[b][t*win_stride + n] (zero past in_len); only its first win_stride
