@@ -495,6 +495,11 @@ __device__ __forceinline__ void ThunderFFT_kernel_reg(vec2_t<T>* __restrict__ re
   if constexpr (detail::mfft::enabled<T, N, batch>) {
     if constexpr (N == 64) detail::mfft::run64<T, forward>(reg, ws, t);
     else detail::mfft::run128<forward>(reg, ws, t);
+  } else if constexpr (detail::mfft::tf32_enabled<T, N, batch>) {
+    float2* r = reinterpret_cast<float2*>(reg);
+    if constexpr (N == 64) detail::mfft::run64_tf32<forward>(r, t);
+    else if constexpr (N == 128) detail::mfft::run128_tf32<forward>(r, t);
+    else detail::mfft::run256_tf32<forward>(r, reinterpret_cast<float2*>(ws), t);
   } else if constexpr (std::is_same_v<T, half>) {
     detail::dfft::run_passes_h<N, batch, F::EPT, F::P, forward, 0, 1>(reg, ws, t);
   } else {

@@ -1,10 +1,15 @@
-// thunderfft_impl_device_mma.cuh — ThunderFFT_kernel_reg for half2 N = 64 (16
-// signals, one warp; and N = 128 on top of it, run128) as two warp-MMA DFT
-// stages, the form of the reference's
-// routine (detail/kernel/shared_kernel_n64_b16.cuh), written for this
-// library's own operand maps.  (The float2 branches below are kept
-// compilable and correct; see `enabled` for why float2 does not use them.)
+// thunderfft_impl_device_mma.cuh — the warp-MMA forms of ThunderFFT_kernel_reg
+// (the reference computes its device routine with warp MMAs too:
+// detail/kernel/unit_kernel_fp32.cuh, unit_kernel_fp16.cuh), each written for
+// this library's own operand maps:
+//   * half2 N = 64 (16 signals, one warp) as two FP16 MMA DFT stages, and
+//     N = 128 on top of it (run64, run128);
+//   * float2 N = 64, 128, 256 with one TF32 MMA radix-4 stage and in-lane
+//     FP32 DFTs (run64_tf32, run128_tf32, run256_tf32, at the end).
+// The run64 template's float2 branches are not used (run64_tf32 serves
+// float2 N = 64).
 //
+// half2 N = 64:
 // Fragment (input and output): lane (gid, tig) = (lane / 4, lane % 4) holds
 // signals gid and gid + 8, elements 16 tig ... 16 tig + 15 of each:
 //   reg[i]: signal gid + 8 (i / 16), element 16 tig + i % 16.
@@ -46,13 +51,12 @@ namespace thunderfft {
 namespace detail {
 namespace mfft {
 
-// The warp-MMA routine serves half2 N = 64 with the API's 16 signals per
-// block: 0.49 us per paper-benchmark call (16384 signals) against 1.02 us for
-// the packed-FP16 register FFT.  Its float2 form (mma.m16n8k8 .tf32, 64 MMAs
-// per call) computes correctly (rel-L2 7.5e-4) at 1.24 us, no faster than
-// the FP32 register FFT, which is also exact to 1e-7, so float2 keeps that.
-// half2 N = 128 (8 signals) reuses it on 16 rows after a radix-2 step
-// (run128).
+// The two-stage warp-MMA routine serves half2 N = 64 with the API's 16
+// signals per block: 0.49 us per paper-benchmark call (16384 signals) against
+// 1.02 us for the packed-FP16 register FFT.  Its float2 form (mma.m16n8k8
+// .tf32, 64 MMAs and a shared-memory exchange per call) measured 1.24 us;
+// run64_tf32 (16 MMAs, no exchange) takes 0.48 us.  half2 N = 128 (8
+// signals) reuses it on 16 rows after a radix-2 step (run128).
 template <typename T, int N, int batch>
 inline constexpr bool enabled =
     std::is_same_v<T, half> && ((N == 64 && batch == 16) || (N == 128 && batch == 8));
@@ -325,6 +329,210 @@ __device__ __forceinline__ void run128(half2* reg, half2* ws, int t) {
       reg[16 * h + 4 * v + 2] = *reinterpret_cast<const half2*>(&q.z);
       reg[16 * h + 4 * v + 3] = *reinterpret_cast<const half2*>(&q.w);
     }
+}
+
+// ---------------------------------------------------------------------------
+// float2 N = 64, 16 signals per warp, TF32 warp MMAs (the reference's float
+// contract: TF32 MMA arithmetic, shared_kernel_n64_b16.cuh).
+//
+// With n = n1 + 16 n2 and k = 4 k1 + k2 (n1, k1 < 16; n2, k2 < 4):
+//   X[4 k1 + k2] = sum_{n1} w_16^(n1 k1) Y[n1][k2],
+//   Y[n1][k2]    = sum_{n2} x[n1 + 16 n2] w_64^((n1 + 16 n2) k2).
+// Input fragment: frag64 (lane (gid, tig) holds n2 = tig, register i holds
+// n1 = i % 16, signals gid and gid + 8).
+//   * Y: one mma.m16n8k8 .tf32 per n1: rows = the 16 signals, K = (re | im of
+//     input n2 = tig), columns = (k2, re | im); the twiddle is in the B
+//     matrix, so lane tig receives Y[n1][k2 = tig] for every n1.  No data
+//     moves between lanes.
+//   * X: the lane's 16-point DFT over n1 (its own k2), radix 4 x 4 in FP32
+//     registers with compile-time roots.
+// Output fragment (frag64_tf32_out): lane (gid, tig), register i holds
+// X[4 (i % 16) + tig] of signal gid + 8 (i / 16).  The inverse runs the same
+// way with conjugate roots, unnormalized.
+template <typename T, int N, int batch>
+inline constexpr bool tf32_enabled =
+    std::is_same_v<T, float> && ((N == 64 && batch == 16) || (N == 128 && batch == 8) || (N == 256 && batch == 16));
+
+__device__ __forceinline__ void frag64_tf32_out(int t, int i, int& j, int& k) {
+  const int lane = t & 31;
+  j = (lane >> 2) + 8 * (i >> 4);
+  k = (lane & 3) + 4 * (i & 15);
+}
+// N = 128 (8 signals): input frag128; output: lane (gid, tig), register i
+// holds X[8 (i % 16) + 2 tig + i / 16] of signal gid.
+__device__ __forceinline__ void frag128_tf32_out(int t, int i, int& j, int& k) {
+  const int lane = t & 31;
+  j = lane >> 2;
+  k = 8 * (i & 15) + 2 * (lane & 3) + (i >> 4);
+}
+// N = 256 (16 signals, 4 warps): warp w, lane (gid, tig), register i holds
+// signal gid + 8 (i / 16): input element 16 w + i % 16 + 64 tig, output
+// element 16 (i % 16) + 4 tig + w.
+__device__ __forceinline__ void frag256_tf32_in(int t, int i, int& j, int& n) {
+  const int lane = t & 31, w = t >> 5;
+  j = (lane >> 2) + 8 * (i >> 4);
+  n = 16 * w + (i & 15) + 64 * (lane & 3);
+}
+__device__ __forceinline__ void frag256_tf32_out(int t, int i, int& j, int& k) {
+  const int lane = t & 31, w = t >> 5;
+  j = (lane >> 2) + 8 * (i >> 4);
+  k = 16 * (i & 15) + 4 * (lane & 3) + w;
+}
+
+// x * w_16^M (forward; conjugate root for the inverse), M a compile-time
+// exponent: 0, 4, 8, 12 need no multiply.
+template <int M, bool fwd>
+__device__ __forceinline__ float2 rot16(float2 x) {
+  constexpr int m = M & 15;
+  if constexpr (m == 0) {
+    return x;
+  } else if constexpr (m == 8) {
+    return make_float2(-x.x, -x.y);
+  } else if constexpr (m == 4 || m == 12) {
+    // w_16^4 = -i (forward), +i (inverse); w_16^12 the opposite
+    constexpr bool minus_i = (m == 4) == fwd;
+    return minus_i ? make_float2(x.y, -x.x) : make_float2(-x.y, x.x);
+  } else {
+    constexpr float c = Root128<8 * m>::c, s = fwd ? -Root128<8 * m>::s : Root128<8 * m>::s;
+    return make_float2(x.x * c - x.y * s, x.x * s + x.y * c);
+  }
+}
+
+// 4-point DFT in place: (u0, u1, u2, u3) -> (U0, U1, U2, U3).
+template <bool fwd>
+__device__ __forceinline__ void dft4(float2& u0, float2& u1, float2& u2, float2& u3) {
+  const float2 s0 = make_float2(u0.x + u2.x, u0.y + u2.y), d0 = make_float2(u0.x - u2.x, u0.y - u2.y);
+  const float2 s1 = make_float2(u1.x + u3.x, u1.y + u3.y), d1 = make_float2(u1.x - u3.x, u1.y - u3.y);
+  u0 = make_float2(s0.x + s1.x, s0.y + s1.y);
+  u2 = make_float2(s0.x - s1.x, s0.y - s1.y);
+  // U1 = d0 + w_4 d1, U3 = d0 - w_4 d1 with w_4 = -i (forward) or +i
+  const float2 wd = fwd ? make_float2(d1.y, -d1.x) : make_float2(-d1.y, d1.x);
+  u1 = make_float2(d0.x + wd.x, d0.y + wd.y);
+  u3 = make_float2(d0.x - wd.x, d0.y - wd.y);
+}
+
+// 16-point DFT of v[0..15] (natural order in and out), radix 4 x 4:
+// n = a + 4 b, k = c + 4 d:  X[c + 4d] = sum_a w_4^(a d) w_16^(a c) sum_b v[a + 4b] w_4^(b c).
+template <bool fwd, int... A>
+__device__ __forceinline__ void twiddle16(float2 (&v)[16], std::integer_sequence<int, A...>) {
+  // v[a + 4c] *= w_16^(a c)
+  ((v[(A & 3) + 4 * (A >> 2)] = rot16<(A & 3) * (A >> 2), fwd>(v[(A & 3) + 4 * (A >> 2)])), ...);
+}
+template <bool fwd>
+__device__ __forceinline__ void dft16(float2 (&v)[16]) {
+#pragma unroll
+  for (int a = 0; a < 4; ++a) dft4<fwd>(v[a], v[a + 4], v[a + 8], v[a + 12]);   // v[a + 4c] = T[a][c]
+  twiddle16<fwd>(v, std::make_integer_sequence<int, 16>{});
+#pragma unroll
+  for (int c = 0; c < 4; ++c) dft4<fwd>(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);   // v[4c + d] = X[c + 4d]
+  float2 o[16];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int d = 0; d < 4; ++d) o[c + 4 * d] = v[4 * c + d];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = o[k];
+}
+
+template <bool fwd>
+__device__ __forceinline__ void run64_tf32(float2* reg, int t) {
+  const int lane = t & 31, gid = lane >> 2, tig = lane & 3;
+  const int k2 = gid >> 1, plane = gid & 1;   // this lane's B column: output k2, re | im
+  float2 y[2][16];
+#pragma unroll
+  for (int n1 = 0; n1 < 16; ++n1) {
+    // B rows tig (re of input n2 = tig) and tig + 4 (im), column gid:
+    // coefficient c = w_64^((n1 + 16 tig) k2) of (re, im) -> (re, im) output
+    const float2 w = unit_root((n1 + 16 * tig) * k2, 64);
+    const float cr = w.x, ci = fwd ? -w.y : w.y;
+    const uint32_t b0 = tf32_bits(plane ? ci : cr), b1 = tf32_bits(plane ? cr : -ci);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    // A: (signal gid | gid + 8) x (re | im of input n2 = tig); the tensor
+    // core reads the TF32 part of each fp32 value
+    mma_tf32(d, __float_as_uint(reg[n1].x), __float_as_uint(reg[16 + n1].x), __float_as_uint(reg[n1].y),
+             __float_as_uint(reg[16 + n1].y), b0, b1);
+    y[0][n1] = make_float2(d[0], d[1]);
+    y[1][n1] = make_float2(d[2], d[3]);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    dft16<fwd>(y[h]);
+#pragma unroll
+    for (int k1 = 0; k1 < 16; ++k1) reg[16 * h + k1] = y[h][k1];   // X[4 k1 + tig]
+  }
+}
+
+// float2 N = 128, 8 signals per warp.  A radix-2 decimation-in-frequency step
+// in registers on frag128 (the lane holds x[n] and x[n + 64] for
+// n = 16 tig + i),
+//   a[n] = x[n] + x[n + 64],  b[n] = (x[n] - x[n + 64]) w_128^n,
+// makes a and b rows gid and gid + 8 of the 64-point routine, whose outputs
+// are A[k] = X[2k] and B[k] = X[2k + 1] (frag128_tf32_out).  No shared memory.
+template <bool fwd, int... I>
+__device__ __forceinline__ void radix2_dif128_f32(float2* reg, float2 wt, std::integer_sequence<int, I...>) {
+  // w_128^(16 tig + i) = w_8^tig (wt, per lane) * w_128^i (compile time)
+  (
+      [&] {
+        constexpr float ci = Root128<I>::c, si = fwd ? -Root128<I>::s : Root128<I>::s;
+        const float wr = wt.x * ci - wt.y * si, wi = wt.x * si + wt.y * ci;
+        const float2 x0 = reg[I], x1 = reg[16 + I];
+        const float dr = x0.x - x1.x, di = x0.y - x1.y;
+        reg[I] = make_float2(x0.x + x1.x, x0.y + x1.y);
+        reg[16 + I] = make_float2(dr * wr - di * wi, dr * wi + di * wr);
+      }(),
+      ...);
+}
+
+template <bool fwd>
+__device__ __forceinline__ void run128_tf32(float2* reg, int t) {
+  const int tig = t & 3;
+  const float2 w8 = unit_root(16 * tig, 128);
+  radix2_dif128_f32<fwd>(reg, make_float2(w8.x, fwd ? -w8.y : w8.y), std::make_integer_sequence<int, 16>{});
+  run64_tf32<fwd>(reg, t);
+}
+
+// float2 N = 256, 16 signals, 4 warps.  With n = n1 + 64 n2, k = 4 k1 + k2:
+//   Y[n1][k2] = sum_{n2} x[n1 + 64 n2] w_256^((n1 + 64 n2) k2)   (one TF32 MMA per n1)
+//   X[4 k1 + k2] = sum_{n1} w_64^(n1 k1) Y[n1][k2]                 (64-point routine)
+// Warp w holds n1 = 16 w + i % 16 for n2 = tig (frag256_tf32_in), computes
+// its Y, and one exchange through the workspace gives warp w all n1 of
+// k2 = w in the 64-point routine's input order.  Exchange position of
+// (signal j, k2, n1): ((64 k2 + n1) 16 + j) with its low bit 3 flipped by
+// bit 0 of (k2 ^ n1 / 16): the stores (k2 = tig) and the loads (n1 / 16 =
+// tig) of one instruction then fill 16 distinct 8-byte bank pairs twice,
+// the minimum of two wavefronts.
+__device__ __forceinline__ int ex256_pos(int j, int k2, int n1) {
+  return (((64 * k2 + n1) << 4) + j) ^ ((((k2 ^ (n1 >> 4)) & 1)) << 3);
+}
+
+template <bool fwd>
+__device__ __forceinline__ void run256_tf32(float2* reg, float2* ws, int t) {
+  const int lane = t & 31, gid = lane >> 2, tig = lane & 3, w = t >> 5;
+  const int k2 = gid >> 1, plane = gid & 1;   // this lane's B column
+  float2 y[2][16];
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const int n1 = 16 * w + m;
+    const float2 c = unit_root((n1 + 64 * tig) * k2, 256);
+    const float cr = c.x, ci = fwd ? -c.y : c.y;
+    const uint32_t b0 = tf32_bits(plane ? ci : cr), b1 = tf32_bits(plane ? cr : -ci);
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_tf32(d, __float_as_uint(reg[m].x), __float_as_uint(reg[16 + m].x), __float_as_uint(reg[m].y),
+             __float_as_uint(reg[16 + m].y), b0, b1);
+    y[0][m] = make_float2(d[0], d[1]);    // Y[n1][k2 = tig], signal gid
+    y[1][m] = make_float2(d[2], d[3]);    // signal gid + 8
+  }
+  __syncthreads();   // the caller may still be reading its workspace
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int m = 0; m < 16; ++m) ws[ex256_pos(gid + 8 * h, tig, 16 * w + m)] = y[h][m];
+  __syncthreads();
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) reg[16 * h + i] = ws[ex256_pos(gid + 8 * h, w, 16 * tig + i)];
+  run64_tf32<fwd>(reg, t);
 }
 
 }  // namespace mfft

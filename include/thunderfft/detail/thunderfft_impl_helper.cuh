@@ -3,8 +3,9 @@
 // Fragment convention of this library: with P = 32 * warp_per_block<N>
 // threads and t = threadIdx.x + 32 * threadIdx.y, thread t holds element
 // e = t + P * i (i < 32) of the block's tile in signal order (e = j*N + n);
-// half2 N = 64 (16 signals) and N = 128 (8 signals) use their MMA operand
-// orders instead (frag_elem).
+// half2 N = 64 (16 signals) and N = 128 (8 signals) and float2 N = 64, 128
+// and 256 use their MMA operand orders instead (frag_elem); the float2
+// output orders differ from their input orders (frag_elem_out).
 // The input fragment holds input elements, the output fragment output
 // elements, both in natural order; the helpers translate to and from any
 // layout_t (strides, periodic padding, digit-reversed shared tiles).
@@ -47,13 +48,29 @@ __device__ __forceinline__ int block_thread() { return threadIdx.x + threadIdx.y
 // order (mfft::frag64, mfft::frag128).
 template <typename T, int N, int batch>
 __device__ __forceinline__ void frag_elem(int t, int i, int& j, int& n) {
-  if constexpr (mfft::enabled<T, N, batch>) {
+  if constexpr (mfft::enabled<T, N, batch> || mfft::tf32_enabled<T, N, batch>) {
     if constexpr (N == 64) mfft::frag64(t, i, j, n);
-    else mfft::frag128(t, i, j, n);
+    else if constexpr (N == 128) mfft::frag128(t, i, j, n);
+    else mfft::frag256_tf32_in(t, i, j, n);
   } else {
     const int e = t + frag<N, batch>::P * i;
     j = e / N;
     n = e % N;
+  }
+}
+
+// Fragment slot i of block thread t in an OUTPUT fragment: the input order
+// (frag_elem), except for the float2 TF32 warp-MMA routines (N = 64, 128,
+// 256), whose outputs leave the last in-lane DFT in the lane that computed
+// it (mfft::frag64_tf32_out, frag128_tf32_out, frag256_tf32_out).
+template <typename T, int N, int batch>
+__device__ __forceinline__ void frag_elem_out(int t, int i, int& j, int& k) {
+  if constexpr (mfft::tf32_enabled<T, N, batch>) {
+    if constexpr (N == 64) mfft::frag64_tf32_out(t, i, j, k);
+    else if constexpr (N == 128) mfft::frag128_tf32_out(t, i, j, k);
+    else mfft::frag256_tf32_out(t, i, j, k);
+  } else {
+    frag_elem<T, N, batch>(t, i, j, k);
   }
 }
 
@@ -105,7 +122,7 @@ __device__ __forceinline__ void ThunderFFT_reg2smem(vec2_t<T>* __restrict__ smem
 #pragma unroll
   for (int i = 0; i < F::EPT; ++i) {
     int j, k;
-    detail::frag_elem<T, sL::N, sL::batch>(t, i, j, k);
+    detail::frag_elem_out<T, sL::N, sL::batch>(t, i, j, k);
     smem[detail::layout_index<sL>(j, detail::stored_position<sL>(k))] = reg[i];
   }
 }

@@ -41,9 +41,10 @@ def test_device_api_composition(cuda, tmp_path):
         assert guard_bad == 0, f.name
         assert np.isfinite(y).all() and np.isfinite(y2).all(), f.name
         e1, e2 = oracle.rel_l2(y, ref), oracle.rel_l2(y2, ref)
-        # the reference's gate for both types; float data is transformed in
-        # FP32 arithmetic here, so it also meets a 1e-5 gate
-        gate = 1e-5 if "_float_" in f.name else 5e-3
+        # the reference's gate for both types; float N <= 256 runs TF32 warp
+        # MMAs (the reference's arithmetic), the larger float sizes FP32
+        # arithmetic, which also meets a 1e-5 gate
+        gate = 1e-5 if ("_float_" in f.name and n > 256) else 5e-3
         assert e1 <= gate and e2 <= gate, (f.name, e1, e2)
 
 

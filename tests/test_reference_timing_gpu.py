@@ -172,5 +172,5 @@ def test_device_api_paper_fft_vs_reference(cuda, prec):
         (ou, oe), (ru, re_) = rows
         print(f"{n:>5} {prec:>5} {ou:8.2f} {ru:7.2f}  {oe:.2e}  {re_:.2e}")
         assert oe <= 5e-3 and re_ <= 5e-3
-        if prec == "tf32":
-            assert oe <= 1e-5  # FP32 arithmetic on this side
+        if prec == "tf32" and n > 256:
+            assert oe <= 1e-5  # FP32 arithmetic on this side (N <= 256: TF32 warp MMAs)
