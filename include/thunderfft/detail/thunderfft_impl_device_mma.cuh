@@ -4,8 +4,8 @@
 // this library's own operand maps:
 //   * half2 N = 64 (16 signals, one warp) as two FP16 MMA DFT stages, and
 //     N = 128 on top of it (run64, run128);
-//   * float2 N = 64, 128, 256 with one TF32 MMA radix-4 stage and in-lane
-//     FP32 DFTs (run64_tf32, run128_tf32, run256_tf32, at the end).
+//   * float2 N = 64, 128, 256 with one TF32 MMA stage (radix 4, 8, 4) and
+//     in-lane FP32 DFTs (run64_tf32, run128_tf32, run256_tf32, at the end).
 // The run64 template's float2 branches are not used (run64_tf32 serves
 // float2 N = 64).
 //
@@ -352,6 +352,9 @@ __device__ __forceinline__ void run128(half2* reg, half2* ws, int t) {
 template <typename T, int N, int batch>
 inline constexpr bool tf32_enabled =
     std::is_same_v<T, float> && ((N == 64 && batch == 16) || (N == 128 && batch == 8) || (N == 256 && batch == 16));
+// routines whose output fragment order differs from the input order
+template <typename T, int N, int batch>
+inline constexpr bool split_order = tf32_enabled<T, N, batch>;
 
 __device__ __forceinline__ void frag64_tf32_out(int t, int i, int& j, int& k) {
   const int lane = t & 31;
@@ -359,11 +362,11 @@ __device__ __forceinline__ void frag64_tf32_out(int t, int i, int& j, int& k) {
   k = (lane & 3) + 4 * (i & 15);
 }
 // N = 128 (8 signals): input frag128; output: lane (gid, tig), register i
-// holds X[8 (i % 16) + 2 tig + i / 16] of signal gid.
+// holds X[8 (i % 16) + 4 (i / 16) + tig] of signal gid.
 __device__ __forceinline__ void frag128_tf32_out(int t, int i, int& j, int& k) {
   const int lane = t & 31;
   j = lane >> 2;
-  k = 8 * (i & 15) + 2 * (lane & 3) + (i >> 4);
+  k = 8 * (i & 15) + 4 * (i >> 4) + (lane & 3);
 }
 // N = 256 (16 signals, 4 warps): warp w, lane (gid, tig), register i holds
 // signal gid + 8 (i / 16): input element 16 w + i % 16 + 64 tig, output
@@ -434,61 +437,108 @@ __device__ __forceinline__ void dft16(float2 (&v)[16]) {
   for (int k = 0; k < 16; ++k) v[k] = o[k];
 }
 
+__device__ __forceinline__ float2 cmulf(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+// B fragment (rows tig: re, tig + 4: im of the lane's input; column: the
+// lane's output, re | im = plane) of the coefficient c.
+__device__ __forceinline__ void b_frag(uint32_t& b0, uint32_t& b1, float2 c, int plane) {
+  b0 = tf32_bits(plane ? c.y : c.x);
+  b1 = tf32_bits(plane ? c.x : -c.y);
+}
+// exp(-+ 2 pi i m / L) (forward: minus)
+template <bool fwd>
+__device__ __forceinline__ float2 root(int m, int L) {
+  const float2 w = unit_root(m, L);
+  return make_float2(w.x, fwd ? -w.y : w.y);
+}
+
 template <bool fwd>
 __device__ __forceinline__ void run64_tf32(float2* reg, int t) {
   const int lane = t & 31, gid = lane >> 2, tig = lane & 3;
   const int k2 = gid >> 1, plane = gid & 1;   // this lane's B column: output k2, re | im
-  float2 y[2][16];
+  // B rows tig (re of input n2 = tig) and tig + 4 (im), column gid: the
+  // coefficient c(n1) = w_64^((n1 + 16 tig) k2) = w_4^(tig k2) w_64^(k2)^n1,
+  // stepped by one complex multiply per n1
+  const float2 q = root<fwd>(k2, 64);
+  float2 c = root<fwd>(16 * tig * k2, 64);
 #pragma unroll
   for (int n1 = 0; n1 < 16; ++n1) {
-    // B rows tig (re of input n2 = tig) and tig + 4 (im), column gid:
-    // coefficient c = w_64^((n1 + 16 tig) k2) of (re, im) -> (re, im) output
-    const float2 w = unit_root((n1 + 16 * tig) * k2, 64);
-    const float cr = w.x, ci = fwd ? -w.y : w.y;
-    const uint32_t b0 = tf32_bits(plane ? ci : cr), b1 = tf32_bits(plane ? cr : -ci);
+    uint32_t b0, b1;
+    b_frag(b0, b1, c, plane);
+    c = cmulf(c, q);
     float d[4] = {0.f, 0.f, 0.f, 0.f};
     // A: (signal gid | gid + 8) x (re | im of input n2 = tig); the tensor
     // core reads the TF32 part of each fp32 value
     mma_tf32(d, __float_as_uint(reg[n1].x), __float_as_uint(reg[16 + n1].x), __float_as_uint(reg[n1].y),
              __float_as_uint(reg[16 + n1].y), b0, b1);
-    y[0][n1] = make_float2(d[0], d[1]);
-    y[1][n1] = make_float2(d[2], d[3]);
+    reg[n1] = make_float2(d[0], d[1]);        // Y[n1][k2 = tig], signal gid (in place)
+    reg[16 + n1] = make_float2(d[2], d[3]);   // signal gid + 8
   }
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
-    dft16<fwd>(y[h]);
+    float2 y[16];
 #pragma unroll
-    for (int k1 = 0; k1 < 16; ++k1) reg[16 * h + k1] = y[h][k1];   // X[4 k1 + tig]
+    for (int n1 = 0; n1 < 16; ++n1) y[n1] = reg[16 * h + n1];
+    dft16<fwd>(y);
+#pragma unroll
+    for (int k1 = 0; k1 < 16; ++k1) reg[16 * h + k1] = y[k1];   // X[4 k1 + tig]
   }
 }
 
-// float2 N = 128, 8 signals per warp.  A radix-2 decimation-in-frequency step
-// in registers on frag128 (the lane holds x[n] and x[n + 64] for
-// n = 16 tig + i),
-//   a[n] = x[n] + x[n + 64],  b[n] = (x[n] - x[n + 64]) w_128^n,
-// makes a and b rows gid and gid + 8 of the 64-point routine, whose outputs
-// are A[k] = X[2k] and B[k] = X[2k + 1] (frag128_tf32_out).  No shared memory.
-template <bool fwd, int... I>
-__device__ __forceinline__ void radix2_dif128_f32(float2* reg, float2 wt, std::integer_sequence<int, I...>) {
-  // w_128^(16 tig + i) = w_8^tig (wt, per lane) * w_128^i (compile time)
-  (
-      [&] {
-        constexpr float ci = Root128<I>::c, si = fwd ? -Root128<I>::s : Root128<I>::s;
-        const float wr = wt.x * ci - wt.y * si, wi = wt.x * si + wt.y * ci;
-        const float2 x0 = reg[I], x1 = reg[16 + I];
-        const float dr = x0.x - x1.x, di = x0.y - x1.y;
-        reg[I] = make_float2(x0.x + x1.x, x0.y + x1.y);
-        reg[16 + I] = make_float2(dr * wr - di * wi, dr * wi + di * wr);
-      }(),
-      ...);
-}
-
+// float2 N = 128, 8 signals per warp, one radix-8 MMA stage.  With
+// n = n1 + 16 n2 and k = 8 k1 + k2 (n1, k1 < 16; n2, k2 < 8):
+//   Y[n1][k2]    = sum_{n2} x[n1 + 16 n2] w_128^((n1 + 16 n2) k2),
+//   X[8 k1 + k2] = sum_{n1} w_16^(n1 k1) Y[n1][k2].
+// frag128 gives the lane n2 = tig (register i) and n2 = tig + 4 (register
+// 16 + i), n1 = i % 16, of signal gid.  Per m < 8, four mma.m16n8k8 (two K
+// steps: n2 < 4, n2 >= 4; two N tiles: k2 < 4, k2 >= 4) with rows (signal
+// gid, n1 = m) and (signal gid, n1 = m + 8); the B matrix holds the
+// twiddle of n1 = m, so the second row half is multiplied by w_128^(8 k2) =
+// w_16^k2 afterwards (k2 = 4 tile + tig, a per-lane root).  The lane then
+// holds all 16 n1 of k2 = tig and tig + 4 and runs two 16-point DFTs.
+// Output (frag128_tf32_out): register i holds X[8 (i % 16) + 4 (i / 16) + tig].
 template <bool fwd>
 __device__ __forceinline__ void run128_tf32(float2* reg, int t) {
-  const int tig = t & 3;
-  const float2 w8 = unit_root(16 * tig, 128);
-  radix2_dif128_f32<fwd>(reg, make_float2(w8.x, fwd ? -w8.y : w8.y), std::make_integer_sequence<int, 16>{});
-  run64_tf32<fwd>(reg, t);
+  const int lane = t & 31, gid = lane >> 2, tig = lane & 3;
+  const int kb = gid >> 1, plane = gid & 1;   // this lane's B column within an N tile
+  // second row half's factor w_16^(4 tile + tig), one per N tile
+  const float2 post0 = root<fwd>(tig, 16), post1 = root<fwd>(4 + tig, 16);
+  // coefficients c(ks, nt, m) = w_128^((m + 16 (4 ks + tig)) (4 nt + kb)),
+  // stepped in m by q(nt) = w_128^(4 nt + kb)
+  const float2 q0 = root<fwd>(kb, 128), q1 = root<fwd>(4 + kb, 128);
+  float2 c00 = root<fwd>(16 * tig * kb, 128), c01 = root<fwd>(16 * tig * (4 + kb), 128);
+  float2 c10 = root<fwd>(16 * (4 + tig) * kb, 128), c11 = root<fwd>(16 * (4 + tig) * (4 + kb), 128);
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    // inputs n1 = m, m + 8 for n2 = tig (ks 0) and tig + 4 (ks 1)
+    const float2 x0 = reg[m], x0h = reg[m + 8], x1 = reg[16 + m], x1h = reg[24 + m];
+    float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t b0, b1;
+    b_frag(b0, b1, c00, plane);
+    mma_tf32(d0, __float_as_uint(x0.x), __float_as_uint(x0h.x), __float_as_uint(x0.y), __float_as_uint(x0h.y), b0, b1);
+    b_frag(b0, b1, c10, plane);
+    mma_tf32(d0, __float_as_uint(x1.x), __float_as_uint(x1h.x), __float_as_uint(x1.y), __float_as_uint(x1h.y), b0, b1);
+    b_frag(b0, b1, c01, plane);
+    mma_tf32(d1, __float_as_uint(x0.x), __float_as_uint(x0h.x), __float_as_uint(x0.y), __float_as_uint(x0h.y), b0, b1);
+    b_frag(b0, b1, c11, plane);
+    mma_tf32(d1, __float_as_uint(x1.x), __float_as_uint(x1h.x), __float_as_uint(x1.y), __float_as_uint(x1h.y), b0, b1);
+    c00 = cmulf(c00, q0); c10 = cmulf(c10, q0); c01 = cmulf(c01, q1); c11 = cmulf(c11, q1);
+    // in place: N tile 0 (k2 = tig) -> registers 0..15, tile 1 (k2 = 4 + tig) -> 16..31
+    reg[m] = make_float2(d0[0], d0[1]);
+    reg[m + 8] = cmulf(make_float2(d0[2], d0[3]), post0);
+    reg[16 + m] = make_float2(d1[0], d1[1]);
+    reg[24 + m] = cmulf(make_float2(d1[2], d1[3]), post1);
+  }
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    float2 y[16];
+#pragma unroll
+    for (int n1 = 0; n1 < 16; ++n1) y[n1] = reg[16 * nt + n1];
+    dft16<fwd>(y);
+#pragma unroll
+    for (int k1 = 0; k1 < 16; ++k1) reg[16 * nt + k1] = y[k1];   // X[8 k1 + 4 nt + tig]
+  }
 }
 
 // float2 N = 256, 16 signals, 4 warps.  With n = n1 + 64 n2, k = 4 k1 + k2:
@@ -509,24 +559,25 @@ template <bool fwd>
 __device__ __forceinline__ void run256_tf32(float2* reg, float2* ws, int t) {
   const int lane = t & 31, gid = lane >> 2, tig = lane & 3, w = t >> 5;
   const int k2 = gid >> 1, plane = gid & 1;   // this lane's B column
-  float2 y[2][16];
+  // c(m) = w_256^((16 w + m + 64 tig) k2), stepped in m by w_256^k2
+  const float2 q = root<fwd>(k2, 256);
+  float2 c = root<fwd>((16 * w + 64 * tig) * k2, 256);
 #pragma unroll
   for (int m = 0; m < 16; ++m) {
-    const int n1 = 16 * w + m;
-    const float2 c = unit_root((n1 + 64 * tig) * k2, 256);
-    const float cr = c.x, ci = fwd ? -c.y : c.y;
-    const uint32_t b0 = tf32_bits(plane ? ci : cr), b1 = tf32_bits(plane ? cr : -ci);
+    uint32_t b0, b1;
+    b_frag(b0, b1, c, plane);
+    c = cmulf(c, q);
     float d[4] = {0.f, 0.f, 0.f, 0.f};
     mma_tf32(d, __float_as_uint(reg[m].x), __float_as_uint(reg[16 + m].x), __float_as_uint(reg[m].y),
              __float_as_uint(reg[16 + m].y), b0, b1);
-    y[0][m] = make_float2(d[0], d[1]);    // Y[n1][k2 = tig], signal gid
-    y[1][m] = make_float2(d[2], d[3]);    // signal gid + 8
+    reg[m] = make_float2(d[0], d[1]);        // Y[n1 = 16 w + m][k2 = tig], signal gid
+    reg[16 + m] = make_float2(d[2], d[3]);   // signal gid + 8
   }
   __syncthreads();   // the caller may still be reading its workspace
 #pragma unroll
   for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int m = 0; m < 16; ++m) ws[ex256_pos(gid + 8 * h, tig, 16 * w + m)] = y[h][m];
+    for (int m = 0; m < 16; ++m) ws[ex256_pos(gid + 8 * h, tig, 16 * w + m)] = reg[16 * h + m];
   __syncthreads();
 #pragma unroll
   for (int h = 0; h < 2; ++h)

@@ -60,12 +60,12 @@ __device__ __forceinline__ void frag_elem(int t, int i, int& j, int& n) {
 }
 
 // Fragment slot i of block thread t in an OUTPUT fragment: the input order
-// (frag_elem), except for the float2 TF32 warp-MMA routines (N = 64, 128,
-// 256), whose outputs leave the last in-lane DFT in the lane that computed
-// it (mfft::frag64_tf32_out, frag128_tf32_out, frag256_tf32_out).
+// (frag_elem), except for the float2 warp-MMA routines (N = 64, 128, 256),
+// which end with an in-lane DFT and leave its outputs in the lane that
+// computed them (mfft::frag64_tf32_out, frag128_tf32_out, frag256_tf32_out).
 template <typename T, int N, int batch>
 __device__ __forceinline__ void frag_elem_out(int t, int i, int& j, int& k) {
-  if constexpr (mfft::tf32_enabled<T, N, batch>) {
+  if constexpr (mfft::split_order<T, N, batch>) {
     if constexpr (N == 64) mfft::frag64_tf32_out(t, i, j, k);
     else if constexpr (N == 128) mfft::frag128_tf32_out(t, i, j, k);
     else mfft::frag256_tf32_out(t, i, j, k);
