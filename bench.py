@@ -764,16 +764,13 @@ def run_conv2d(args):
     one thff_conv2d call per step; no collective touches image data."""
     import torch
     import thunderfft_b200 as tf
-    from thunderfft_b200.shard import shard_range
+    from thunderfft_b200.shard import conv2d_image_shard
 
     ranks = Ranks()
     world, rank, dev = ranks.world, ranks.rank, ranks.dev
     stream = torch.cuda.current_stream(dev)
     tf.conv2d_set_arithmetic(args.conv_arith)
-    if args.scaling == "strong":
-        b0, nb = shard_range(CONV2D_B, world, rank, align=2)
-    else:
-        b0, nb = 0, CONV2D_B
+    b0, nb = conv2d_image_shard(CONV2D_B, world, rank, args.scaling)
     C, hw, f = CONV2D_C, CONV2D_HW, CONV2D_F
     g = torch.Generator(device=dev)
     g.manual_seed(4321)   # the same filters on every rank

@@ -108,7 +108,7 @@ thff_status thff_test_inject_cuda_error(int cuda_error, int skip);
  * (sample/conv1d/conv1d_fullfft_l4096_thunder.cu:280-331), here for float
  * storage.  For each of `batch` real
  * signals x[b] of length `lin` (zero-padded to n) and one real filter h:
- *     y[b][m] = (1/n) * sum_k x[b][(m-k) mod n] * h[k],   m < n,
+ *     y[b][m] = sum_k x[b][(m-k) mod n] * h[k],   m < n,
  * computed as FFT -> multiply by the filter spectrum -> inverse FFT in ONE
  * kernel.  n in {1024, 4096}; lin <= n and a multiple of sqrt(n); x must be
  * 16-byte aligned; y holds batch*n floats.  With lin + taps - 1 <= n the

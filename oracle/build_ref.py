@@ -14,6 +14,9 @@ Against the REFERENCE's own headers (the reference as it is):
   ref_conv1d_tiled        the tiled conv1d sample (sample/conv1d/main.cu);
   ref_conv1d_full         the fused FFT-conv sample
                           (sample/conv1d/conv1d_fullfft_l4096_thunder.cu);
+  ref_conv1d_io           oracle/ref_conv1d_io.cu: that sample's fused kernel
+                          run on inputs read from a file, for parity of the
+                          conv1d on identical signals and taps;
   ref_paper_fft           the device-API timing CLI (sample/bench/paper_fft.cu,
                           with its util/ and baseline/ include directories and
                           --use_fast_math, as its CMakeLists builds it).
@@ -49,10 +52,11 @@ OUT_DIR = HERE / "_ref"
 OUT = OUT_DIR / "libthff_ref.so"
 OUT_INPUTS = OUT_DIR / "libthff_ref_inputs.so"
 VALIDATION_SRC = REF / "sample" / "validation" / "fft_validation.cu"
+CONV1D_SRC = REF / "sample" / "conv1d" / "conv1d_fullfft_l4096_thunder.cu"
 
 SAMPLES = {
     "ref_conv1d_tiled": REF / "sample" / "conv1d" / "main.cu",
-    "ref_conv1d_full": REF / "sample" / "conv1d" / "conv1d_fullfft_l4096_thunder.cu",
+    "ref_conv1d_full": CONV1D_SRC,
     "ref_paper_fft": REF / "sample" / "bench" / "paper_fft.cu",
 }
 EXTRA_FLAGS = {
@@ -129,6 +133,13 @@ def main() -> int:
     for name, sample in SAMPLES.items():
         if sample.exists():
             build_sample(name, sample)
+    src, out = HERE / "ref_conv1d_io.cu", OUT_DIR / "ref_conv1d_io"
+    if CONV1D_SRC.exists() and stale(out, src, CONV1D_SRC):
+        tmp = out.with_suffix(".tmp")
+        subprocess.run([NVCC, "-std=c++17", "-O3", *ARCH, "-I", str(REF_INCLUDE), "-I", str(CONV1D_SRC.parent),
+                        f'-DTHFF_REF_CONV1D_SOURCE="{CONV1D_SRC}"', str(src), "-lcufft", "-o", str(tmp)], check=True)
+        tmp.replace(out)
+        print(out)
     for name, (sample, libs) in REFVAL.items():
         if sample.exists():
             build_refval(name, sample, libs)

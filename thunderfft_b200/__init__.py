@@ -250,7 +250,7 @@ def conv1d_filter_spectrum(h, n: int, stream=None):
 def conv1d(x, spectrum, n: int, out=None, stream=None, sync: bool = True):
     """Fused real circular convolution of every row of x (float32 CUDA tensor
     [batch, lin], zero-padded to n) with the filter whose spectrum is given:
-    out[b, m] = (1/n) sum_k x[b][(m-k) mod n] h[k] (one kernel: FFT, multiply,
+    out[b, m] = sum_k x[b][(m-k) mod n] h[k] (one kernel: FFT, multiply,
     inverse FFT).  Returns out [batch, n] float32."""
     import torch
 

@@ -29,6 +29,20 @@ def shard_range(batch: int, world: int, rank: int, align: int = 1):
     return start, stop - start
 
 
+def conv2d_image_shard(batch_images: int, world: int, rank: int, scaling: str = "strong"):
+    """Batch images [b0, b0 + nb) that `rank` convolves in the 2-D convolution.
+
+    strong: the batch is split by image pair (images b and b + 1 of a channel
+    share one complex transform), so every slice starts on an even image and
+    only the batch's odd last image can stand alone; weak: every rank takes
+    the whole batch."""
+    if scaling == "weak":
+        return 0, batch_images
+    if scaling != "strong":
+        raise ValueError("scaling must be 'strong' or 'weak'")
+    return shard_range(batch_images, world, rank, align=2)
+
+
 def weak_scaling_value(bytes_per_rank: float, max_ms: float, world: int) -> float:
     """Whole-job throughput (GB/s) when every rank moves `bytes_per_rank`
     bytes and the slowest rank took `max_ms` milliseconds."""
