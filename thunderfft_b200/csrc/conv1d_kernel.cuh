@@ -63,8 +63,15 @@ struct Conv1dCfg {
   static constexpr uint32_t SMEM_BYTES = exclusive_smem(OFF_B + 3 * BT_BYTES + 1024);
   static_assert(SMEM_BYTES + 1024 <= 232448, "shared memory budget");
   static_assert(M == 128 ? NCOL <= 128 : NCOL <= 256, "TMEM budget (4 accumulators)");
-  static constexpr int kThreads = kMixed ? 352 : 320;  // + range-scale warp (kMixed)
-  static constexpr int kBlocks = M / 64;                 // 16-row blocks per epilogue warp
+  // Two epilogue warps per TMEM lane quadrant and group: each takes two of a
+  // stage's four accumulator pieces (N = 4096: one of the quadrant's two
+  // 16-row blocks), so four warps per scheduler hide the epilogues' TMEM,
+  // shared-memory and FMA latencies.
+  static constexpr int EPW = 2;
+  static constexpr int kGroupWarps = 4 * EPW;            // per epilogue group
+  static constexpr int kThreads = 32 * (2 + 2 * kGroupWarps + (kMixed ? 1 : 0));   // + range-scale warp
+  static constexpr int kBlocks = M / 64;                 // 16-row blocks per TMEM lane quadrant
+  static constexpr int kWarpBlocks = (L == 64) ? kBlocks / EPW : kBlocks;   // blocks one epilogue warp owns
 };
 
 struct Conv1dParams {
@@ -124,11 +131,11 @@ struct Conv1dShared {
 // and the last epilogue multiplies by 1/(s1 s2 s3).
 template <class C, int S>
 __device__ __forceinline__ bool conv1d_epilogue(const Conv1dParams& p, int j, uint32_t tmem, const Conv1dShared& sh,
-                                                uint32_t q, uint32_t lane, int l4,
-                                                const int (&ksv)[C::kBlocks],
-                                                const float4 (&cst)[C::kBlocks][C::L / 8],
-                                                const uint32_t (&ba)[C::kBlocks][4],
-                                                const uint32_t (&bb)[C::kBlocks][8]) {
+                                                uint32_t q, uint32_t lane, int l4, int hw,
+                                                const int (&ksv)[C::kWarpBlocks],
+                                                const float4 (&cst)[C::kWarpBlocks][C::L / 8],
+                                                const uint32_t (&ba)[C::kWarpBlocks][4],
+                                                const uint32_t (&bb)[C::kWarpBlocks][8]) {
   using namespace sm100;
   constexpr int kB = C::kBlocks;
   constexpr bool kInverse = S >= 2;
@@ -154,9 +161,13 @@ __device__ __forceinline__ bool conv1d_epilogue(const Conv1dParams& p, int j, ui
   const uint32_t bdst = smem_u32(sh.bbuf + (S < 3 ? S : 0) * C::BT_BYTES);
   // The accumulator is read in four pieces of 32 registers (re and im planes
   // of four index pairs u): L = 64 -> (block, half of the u range), L = 32 ->
-  // (signal c).  The load of piece i+1 is in flight while piece i is
-  // processed (tcgen05.wait::ld waits for all outstanding loads).
+  // (signal c).  Epilogue warp hw of its quadrant takes pieces 2 hw and
+  // 2 hw + 1 (L = 64: block hw, whose constants are its block 0).  The load
+  // of each piece completes before it is processed; with four epilogue
+  // warps per scheduler the other warps cover that latency (a second buffer
+  // in flight measured the same and spilled under the 96-register cap).
   static_assert(kB * C::TC * (C::L / 32) == 4, "four accumulator pieces per stage");
+  static_assert(C::EPW == 2, "two pieces per epilogue warp");
   auto load_piece = [&](int pc, uint32_t (&v)[32]) {
     if constexpr (C::L == 64) {
       const uint32_t a = detail::acc_addr<C>(tmem, S, q, pc >> 1) + 32u * (uint32_t)(pc & 1);
@@ -166,15 +177,14 @@ __device__ __forceinline__ bool conv1d_epilogue(const Conv1dParams& p, int j, ui
       tmem_ld_16x256b_x8(detail::acc_addr<C>(tmem, S, q, 0) + (uint32_t)(pc * 2 * C::L), v);
     }
   };
-  uint32_t vbuf[2][32];
-  load_piece(0, vbuf[0]);
-  tmem_wait_ld();
-  tmem_regs_ready(vbuf[0]);
 #pragma unroll
-  for (int pc = 0; pc < 4; ++pc) {
-    if (pc < 3) load_piece(pc + 1, vbuf[(pc + 1) & 1]);
-    const uint32_t (&v)[32] = vbuf[pc & 1];   // v[0..15]: re plane, v[16..31]: im plane
-    const int bi = (C::L == 64) ? (pc >> 1) : 0;
+  for (int pp = 0; pp < 2; ++pp) {
+    const int pc = 2 * hw + pp;
+    uint32_t v[32];   // v[0..15]: re plane, v[16..31]: im plane
+    load_piece(pc, v);
+    tmem_wait_ld();
+    tmem_regs_ready(v);
+    const int bi = 0;                       // the warp's own block (L = 64) or the only one
     const int c = (C::L == 64) ? 0 : pc;
     const int u0 = (C::L == 64) ? 4 * (pc & 1) : 0;
     // column-atom offsets of signal c (f32: its re / im planes)
@@ -240,10 +250,6 @@ __device__ __forceinline__ bool conv1d_epilogue(const Conv1dParams& p, int j, ui
         if (yim) *reinterpret_cast<float2*>(yim + 8 * u) = make_float2(yi[0] * scale, yi[1] * scale);
       }
     }
-    if (pc < 3) {
-      tmem_wait_ld();
-      tmem_regs_ready(vbuf[(pc + 1) & 1]);
-    }
   }
   tc_fence_before();
   if (S < 3) fence_proxy_async_smem();
@@ -262,14 +268,16 @@ __device__ __forceinline__ bool conv1d_epilogue(const Conv1dParams& p, int j, ui
 template <class C, bool kGroupA>
 __device__ __forceinline__ void conv1d_epilogue_group(const Conv1dParams& p, int T, uint32_t tmem,
                                                       const Conv1dShared& sh, uint32_t warp, uint32_t lane,
-                                                      float spec_scale) {
+                                                      int hw, float spec_scale) {
   const uint32_t q = warp & 3u;
   const int l4 = (int)(lane & 3u);
   constexpr int kU = C::L / 8;
-  constexpr int kB = C::kBlocks;
+  constexpr int kB = C::kWarpBlocks;
   int ksv[kB];
+  // the warp's 16-row blocks: M = 128 (L = 64) -> block hw of the quadrant's
+  // two; M = 64 -> the quadrant's only block
 #pragma unroll
-  for (int bi = 0; bi < kB; ++bi) ksv[bi] = ((C::M == 64) ? (int)q : (int)(2 * q + bi)) * 8 + (int)(lane >> 2);
+  for (int bi = 0; bi < kB; ++bi) ksv[bi] = ((C::M == 64) ? (int)q : (int)(2 * q) + hw) * 8 + (int)(lane >> 2);
   // group A: forward twiddles w_N^-(a ks) of its pairs (inverse = conjugate);
   // group B: spectrum values H[L ka + i0 + o] (ka = ks) as float4 pairs.
   float4 cst[kB][kU];
@@ -322,11 +330,12 @@ __device__ __forceinline__ void conv1d_epilogue_group(const Conv1dParams& p, int
   for (int r = 0; r < T + 3; ++r) {
     bool ok = true;
     if constexpr (kGroupA) {
-      if (r < T) ok = conv1d_epilogue<C, 0>(p, r, tmem, sh, q, lane, l4, ksv, cst, ba, bb);
-      if (ok && r >= 2 && r - 2 < T) ok = conv1d_epilogue<C, 2>(p, r - 2, tmem, sh, q, lane, l4, ksv, cst, ba, bb);
+      if (r < T) ok = conv1d_epilogue<C, 0>(p, r, tmem, sh, q, lane, l4, hw, ksv, cst, ba, bb);
+      if (ok && r >= 2 && r - 2 < T)
+        ok = conv1d_epilogue<C, 2>(p, r - 2, tmem, sh, q, lane, l4, hw, ksv, cst, ba, bb);
     } else {
-      if (r >= 1 && r - 1 < T) ok = conv1d_epilogue<C, 1>(p, r - 1, tmem, sh, q, lane, l4, ksv, cst, ba, bb);
-      if (ok && r >= 3) ok = conv1d_epilogue<C, 3>(p, r - 3, tmem, sh, q, lane, l4, ksv, cst, ba, bb);
+      if (r >= 1 && r - 1 < T) ok = conv1d_epilogue<C, 1>(p, r - 1, tmem, sh, q, lane, l4, hw, ksv, cst, ba, bb);
+      if (ok && r >= 3) ok = conv1d_epilogue<C, 3>(p, r - 3, tmem, sh, q, lane, l4, hw, ksv, cst, ba, bb);
     }
     if (!ok) break;
   }
@@ -356,8 +365,8 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
     for (int i = 0; i < C::SIN; ++i) {
       mbar_init(&bar_in_full[i], 1); mbar_init(&bar_in_empty[i], C::kF16 ? 2 : 1); mbar_init(&bar_scale[i], 1);
     }
-    for (int i = 0; i < 4; ++i) { mbar_init(&bar_d_full[i], 1); mbar_init(&bar_d_empty[i], 4); }
-    for (int i = 0; i < 3; ++i) { mbar_init(&bar_b_full[i], 4); mbar_init(&bar_b_empty[i], 1); }
+    for (int i = 0; i < 4; ++i) { mbar_init(&bar_d_full[i], 1); mbar_init(&bar_d_empty[i], C::kGroupWarps); }
+    for (int i = 0; i < 3; ++i) { mbar_init(&bar_b_full[i], C::kGroupWarps); mbar_init(&bar_b_empty[i], 1); }
     mbar_init(&bar_const, 1);
     mbar_init(&bar_done, 1);
     spec_max_bits = 0u;
@@ -465,10 +474,11 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
       mbar_wait(&bar_done, 0, p.err, kDevTimeoutMma);
     }
     __syncwarp();
-  } else if (warp < 10) {
+  } else if (warp < 2 + 2 * C::kGroupWarps) {
     // ------------------------------------------------------------ epilogues
-    // group A (warps 2-5): E1 (D0 -> B2) and E3 (D2 -> B4)
-    // group B (warps 6-9): E2 (D1 -> *H -> B3) and E4 (D3 -> y)
+    // group A (warps 2-9): E1 (D0 -> B2) and E3 (D2 -> B4)
+    // group B (warps 10-17): E2 (D1 -> *H -> B3) and E4 (D3 -> y)
+    // (two warps per TMEM lane quadrant in each group, hw = 0, 1)
     // Thread (q = warp % 4, lane) owns, per 16-row block bi, the row pair
     // ks = block*8 + lane/4 and the index pairs (i0, i0+1), i0 = 8u + 2*l4,
     // u < L/8.  Everything that depends only on (ks, l4) — twiddles or
@@ -486,8 +496,10 @@ conv1d_kernel(const __grid_constant__ CUtensorMap tmap_x, const Conv1dParams p) 
       sh.e3 = -detail::ceil_log2f((float)C::L * 1.41421357f);
       spec_scale = detail::pow2f(sh.e2);
     }
-    if (warp < 6) conv1d_epilogue_group<C, true>(p, T, tmem, sh, warp, lane, spec_scale);
-    else conv1d_epilogue_group<C, false>(p, T, tmem, sh, warp, lane, spec_scale);
+    const bool group_a = warp < 2 + C::kGroupWarps;
+    const int hw = (int)((warp - 2 - (group_a ? 0 : C::kGroupWarps)) >> 2);
+    if (group_a) conv1d_epilogue_group<C, true>(p, T, tmem, sh, warp, lane, hw, spec_scale);
+    else conv1d_epilogue_group<C, false>(p, T, tmem, sh, warp, lane, hw, spec_scale);
   } else if constexpr (C::kF16) {
     // ------------------------------------------------------------ range scale
     // Per input tile: max |x| over its real signals -> exponent of the
