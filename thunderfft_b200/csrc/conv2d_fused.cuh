@@ -119,11 +119,91 @@ struct AccGeo {
   static constexpr int BPW = (kM == 64) ? 1 : 2 / kEPW;
   static constexpr int CH = (kM == 64) ? kNC / kEPW : kNC;
   static_assert(kM == 64 ? kNC % kEPW == 0 : 2 % kEPW == 0, "epilogue split");
-  __device__ static int ch0(int h) { return (kM == 64 && kEPW > 1) ? h * CH : 0; }
-  __device__ static int block(uint32_t q, int h, int bi) { return (kM == 64) ? (int)q : (int)(2 * q) + h * BPW + bi; }
+  __host__ __device__ static constexpr int ch0(int h) { return (kM == 64 && kEPW > 1) ? h * CH : 0; }
+  __host__ __device__ static constexpr int block(uint32_t q, int h, int bi) {
+    return (kM == 64) ? (int)q : (int)(2 * q) + h * BPW + bi;
+  }
   __device__ static uint32_t lanes(uint32_t q, int h, int bi, uint32_t loff) {
     return (kM == 64) ? 32u * q + loff : 32u * q + 16u * (uint32_t)(h * BPW + bi);
   }
+};
+
+// Write addresses of the four epilogues as functions of (warp, lane, row
+// block bi, chunk c, 8-column group o) for epi::addr_kind (epi_addr.cuh).
+// Group A is warps [2, 2 + kEpiWarps), group B the next kEpiWarps.
+template <class C>
+struct Conv2dColAddr {
+  using D = typename C::D;
+  // E1: byte offset in B2 of the twiddled stage-1 output
+  struct E1 {
+    __host__ __device__ static constexpr uint32_t f(int warp, int lane, int bi, int c, int o) {
+      using G = AccGeo<C::M1, C::N1, C::EPW>;
+      const int q = warp & 3, h = (warp - 2) >> 2, l4 = lane & 3;
+      const int rp = G::block((uint32_t)q, h, bi) * 8 + (lane >> 2);
+      const int g1 = rp / C::NS, ks = rp % C::NS;
+      const int pidx = 4 * ((G::ch0(h) + c) * 8 + o) + l4;
+      const int a = pidx / C::C1, c1 = pidx % C::C1;
+      const int sig = g1 * C::C1 + c1;
+      const int g2 = sig / C::C2, c2 = sig % C::C2;
+      const uint32_t krow = (uint32_t)detail::stage2_krow(C::R2, g2 * C::NA + a);
+      const int col = c2 * 2 * C::NS + 2 * (C::kColPairs2 ? detail::stage2_col_pair(ks) : ks);
+      return (uint32_t)(col / C::E) * C::LBO2 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
+    }
+  };
+  // E3: byte offset in B4 of the twiddled inverse stage-1 output
+  struct E3 {
+    __host__ __device__ static constexpr uint32_t f(int warp, int lane, int bi, int c, int o) {
+      using G = AccGeo<C::M2, C::N2, C::EPW>;
+      const int q = warp & 3, h = (warp - 2) >> 2, l4 = lane & 3;
+      const int rp = G::block((uint32_t)q, h, bi) * 8 + (lane >> 2);
+      const int g3 = rp / C::NA, ksp = rp % C::NA;
+      const int pidx = 4 * ((G::ch0(h) + c) * 8 + o) + l4;
+      const int c3 = pidx / C::NS, ap = pidx % C::NS;
+      const int sig = g3 * C::C2 + c3;
+      const int g4 = sig / C::C1, c4 = sig % C::C1;
+      const uint32_t krow = (uint32_t)detail::stage2_krow(C::R2, g4 * C::NS + ap);
+      const int col = c4 * 2 * C::NA + 2 * detail::stage2_col_pair(ksp);
+      return (uint32_t)(col / C::E) * C::LBO1 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
+    }
+  };
+  // E2 (column pairs, o even): kWhat 0: byte offset in B3 of outputs k0,
+  // k0 + 1; 1: their 128-B-swizzled byte offset in the staged spectrum tile
+  template <int kWhat>
+  struct E2 {
+    __host__ __device__ static constexpr uint32_t f(int warp, int lane, int bi, int c, int o) {
+      using G = AccGeo<C::M2, C::N2, C::EPW>;
+      const int q = warp & 3, h = (warp - 2 - C::kEpiWarps) >> 2, l4 = lane & 3;
+      const int rp = G::block((uint32_t)q, h, bi) * 8 + (lane >> 2);
+      const int g2 = rp / C::NA, ka = rp % C::NA;
+      const int pidx = 4 * ((G::ch0(h) + c) * 8 + o) + l4;
+      const int c2 = pidx / C::NS, pp = pidx % C::NS;
+      const int ks0 = (pp & ~7) + 2 * l4;
+      if (kWhat == 1) {
+        const uint32_t byte = (uint32_t)((g2 * C::C2 + c2) * C::N + C::NS * ka + ks0) * 8u;
+        return byte ^ (((byte >> 7) & 7u) << 4);
+      }
+      const uint32_t krow = (uint32_t)detail::stage2_krow(C::R2, g2 * C::NA + ka);
+      const int col = c2 * 2 * C::NS + 2 * ks0;
+      return (uint32_t)(col / C::E) * C::LBO2 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
+    }
+  };
+  // E4 (o even), column-blocked output with block width 4: kWhat 0: m0 >> 2
+  // (the block row of output row m0); 1: sl * 4 + (m0 & 3).  The element
+  // offset is then (m0 >> 2) * rows * 4 + the kWhat-1 value + the tile base.
+  template <int kWhat>
+  struct E4 {
+    __host__ __device__ static constexpr uint32_t f(int warp, int lane, int bi, int c, int o) {
+      using G = AccGeo<C::M1, C::N1, C::EPW>;
+      const int q = warp & 3, h = (warp - 2 - C::kEpiWarps) >> 2, l4 = lane & 3;
+      const int rp = G::block((uint32_t)q, h, bi) * 8 + (lane >> 2);
+      const int g4 = rp / C::NS, kap = rp % C::NS;
+      const int pidx = 4 * ((G::ch0(h) + c) * 8 + o) + l4;
+      const int c4 = pidx / C::NA, pp = pidx % C::NA;
+      const int m0 = C::NA * kap + (pp & ~7) + 2 * l4;
+      const int sl = g4 * C::C1 + c4;
+      return kWhat == 0 ? (uint32_t)(m0 >> 2) : (uint32_t)(sl * 4 + (m0 & 3));
+    }
+  };
 };
 
 struct Conv2dColShared {
@@ -178,6 +258,20 @@ __device__ __forceinline__ void conv2d_cols_group_a(const FftParams& p, int ntil
   }
   const uint32_t b2 = smem_u32(sh.smem + C::OFF_B);
   const uint32_t b4 = b2 + 2u * C::TILE_BYTES;
+  // store addresses: per-thread bases plus compile-time offsets (epi_addr.cuh)
+  using A1 = typename Conv2dColAddr<C>::E1;
+  using A3 = typename Conv2dColAddr<C>::E3;
+  constexpr int kK1 = epi::addr_kind<A1, 2, C::kEpiWarps, G1g::BPW, G1g::CH, 8>();
+  constexpr int kK3 = epi::addr_kind<A3, 2, C::kEpiWarps, G3g::BPW, G3g::CH, 8>();
+  uint32_t base1[G1g::BPW][kK1 == 1 ? 8 : 1], base3[G3g::BPW][kK3 == 1 ? 8 : 1];
+#pragma unroll
+  for (int bi = 0; bi < G1g::BPW; ++bi)
+#pragma unroll
+    for (int o = 0; o < (kK1 == 1 ? 8 : 1); ++o) base1[bi][o] = b2 + A1::f((int)warp, (int)lane, bi, 0, o);
+#pragma unroll
+  for (int bi = 0; bi < G3g::BPW; ++bi)
+#pragma unroll
+    for (int o = 0; o < (kK3 == 1 ? 8 : 1); ++o) base3[bi][o] = b4 + A3::f((int)warp, (int)lane, bi, 0, o);
 
   for (int r = 0; r < ntiles + 2; ++r) {
     // ---------------------------------------------------------------- E1(r)
@@ -186,18 +280,27 @@ __device__ __forceinline__ void conv2d_cols_group_a(const FftParams& p, int ntil
       if (!mbar_wait_warp(&sh.d_full[0], ph, p.err, kDevTimeoutEpilogue)) return;
       if (!mbar_wait_warp(&sh.b_empty[0], ph ^ 1u, p.err, kDevTimeoutEpilogue)) return;
       tc_fence_after();
+      // 32-column TMEM pieces, the next one loading while this one is processed
+      constexpr int kNIT1 = G1g::BPW * G1g::CH * 2;
+      auto taddr1 = [&](int it) -> uint32_t {
+        const int bi = it / (2 * G1g::CH), c = (it / 2) % G1g::CH, hh = it & 1;
+        return tmem + (G1g::lanes(q, h, bi, C::lane_off(C::M1, 0)) << 16) + C::col_off(C::M1, 0, 0) + (uint32_t)(ch01 + c) * 64u + 32u * (uint32_t)hh;
+      };
+      uint32_t vb[2][16];
+      tmem_ld_16x256b_x4(taddr1(0), vb[0]);
 #pragma unroll
       for (int bi = 0; bi < G1g::BPW; ++bi) {
         const int rp = G1g::block(q, h, bi) * 8 + (int)(lane >> 2);
         const int g1 = rp / C::NS, ks = rp % C::NS;
-        const uint32_t base = tmem + (G1g::lanes(q, h, bi, C::lane_off(C::M1, 0)) << 16) + C::col_off(C::M1, 0, 0);
 #pragma unroll
         for (int c = 0; c < G1g::CH; ++c) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {   // two 32-column loads: 16 registers in flight
-          uint32_t v[16];
-          tmem_ld_16x256b_x4(base + (uint32_t)(ch01 + c) * 64u + 32u * (uint32_t)hh, v);
+          const int it = (bi * G1g::CH + c) * 2 + hh;
           tmem_wait_ld();
+          tmem_regs_ready(vb[it & 1]);
+          if (it + 1 < kNIT1) tmem_ld_16x256b_x4(taddr1(it + 1), vb[(it + 1) & 1]);
+          const uint32_t (&v)[16] = vb[it & 1];
 #pragma unroll
           for (int oo = 0; oo < 4; ++oo) {
             const int o = 4 * hh + oo;
@@ -208,12 +311,17 @@ __device__ __forceinline__ void conv2d_cols_group_a(const FftParams& p, int ntil
             const float yr = RR - II, yi = IR + RI;
             const float2 w = tw1[bi][(c * 8 + o) / kTq1];
             const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
-            const int sig = g1 * C::C1 + c1;
-            const int g2 = sig / C::C2, c2 = sig % C::C2;
-            const uint32_t krow = (uint32_t)detail::stage2_krow(C::R2, g2 * C::NA + a);
-            const int col = c2 * 2 * C::NS + 2 * (C::kColPairs2 ? detail::stage2_col_pair(ks) : ks);
-            const uint32_t off = (uint32_t)(col / C::E) * C::LBO2 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
-            detail::store_complex<C::kIsHalf>(b2 + off, zr, zi);
+            uint32_t addr;
+            if constexpr (kK1 != 0) {
+              addr = base1[bi][kK1 == 1 ? o : 0] + epi::addr_delta<A1, 2, kK1>(bi, c, o);
+            } else {
+              const int sig = g1 * C::C1 + c1;
+              const int g2 = sig / C::C2, c2 = sig % C::C2;
+              const uint32_t krow = (uint32_t)detail::stage2_krow(C::R2, g2 * C::NA + a);
+              const int col = c2 * 2 * C::NS + 2 * (C::kColPairs2 ? detail::stage2_col_pair(ks) : ks);
+              addr = b2 + (uint32_t)(col / C::E) * C::LBO2 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
+            }
+            detail::store_complex<C::kIsHalf>(addr, zr, zi);
           }
           }
         }
@@ -230,18 +338,27 @@ __device__ __forceinline__ void conv2d_cols_group_a(const FftParams& p, int ntil
       if (!mbar_wait_warp(&sh.d_full[2], ph, p.err, kDevTimeoutEpilogue)) return;
       if (!mbar_wait_warp(&sh.b_empty[2], ph ^ 1u, p.err, kDevTimeoutEpilogue)) return;
       tc_fence_after();
+      // 32-column TMEM pieces, the next one loading while this one is processed
+      constexpr int kNIT3 = G3g::BPW * G3g::CH * 2;
+      auto taddr3 = [&](int it) -> uint32_t {
+        const int bi = it / (2 * G3g::CH), c = (it / 2) % G3g::CH, hh = it & 1;
+        return tmem + (G3g::lanes(q, h, bi, C::lane_off(C::M2, 1)) << 16) + C::col_off(C::M2, 1, 1) + (uint32_t)(ch03 + c) * 64u + 32u * (uint32_t)hh;
+      };
+      uint32_t vb[2][16];
+      tmem_ld_16x256b_x4(taddr3(0), vb[0]);
 #pragma unroll
       for (int bi = 0; bi < G3g::BPW; ++bi) {
         const int rp = G3g::block(q, h, bi) * 8 + (int)(lane >> 2);
         const int g3 = rp / C::NA, ksp = rp % C::NA;
-        const uint32_t base = tmem + (G3g::lanes(q, h, bi, C::lane_off(C::M2, 1)) << 16) + C::col_off(C::M2, 1, 1);
 #pragma unroll
         for (int c = 0; c < G3g::CH; ++c) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {   // two 32-column loads: 16 registers in flight
-          uint32_t v[16];
-          tmem_ld_16x256b_x4(base + (uint32_t)(ch03 + c) * 64u + 32u * (uint32_t)hh, v);
+          const int it = (bi * G3g::CH + c) * 2 + hh;
           tmem_wait_ld();
+          tmem_regs_ready(vb[it & 1]);
+          if (it + 1 < kNIT3) tmem_ld_16x256b_x4(taddr3(it + 1), vb[(it + 1) & 1]);
+          const uint32_t (&v)[16] = vb[it & 1];
 #pragma unroll
           for (int oo = 0; oo < 4; ++oo) {
             const int o = 4 * hh + oo;
@@ -252,12 +369,17 @@ __device__ __forceinline__ void conv2d_cols_group_a(const FftParams& p, int ntil
             const float yr = RR + II, yi = RI - IR;     // inverse: sine terms flipped
             const float2 w = tw3[bi][(c * 8 + o) % kTw3];
             const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
-            const int sig = g3 * C::C2 + c3;
-            const int g4 = sig / C::C1, c4 = sig % C::C1;
-            const uint32_t krow = (uint32_t)detail::stage2_krow(C::R2, g4 * C::NS + ap);
-            const int col = c4 * 2 * C::NA + 2 * detail::stage2_col_pair(ksp);
-            const uint32_t off = (uint32_t)(col / C::E) * C::LBO1 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
-            detail::store_complex<C::kIsHalf>(b4 + off, zr, zi);
+            uint32_t addr;
+            if constexpr (kK3 != 0) {
+              addr = base3[bi][kK3 == 1 ? o : 0] + epi::addr_delta<A3, 2, kK3>(bi, c, o);
+            } else {
+              const int sig = g3 * C::C2 + c3;
+              const int g4 = sig / C::C1, c4 = sig % C::C1;
+              const uint32_t krow = (uint32_t)detail::stage2_krow(C::R2, g4 * C::NS + ap);
+              const int col = c4 * 2 * C::NA + 2 * detail::stage2_col_pair(ksp);
+              addr = b4 + (uint32_t)(col / C::E) * C::LBO1 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
+            }
+            detail::store_complex<C::kIsHalf>(addr, zr, zi);
           }
           }
         }
@@ -290,6 +412,33 @@ __device__ __forceinline__ void conv2d_cols_group_b(const FftParams& p, int ntil
   const uint32_t b3 = smem_u32(sh.smem + C::OFF_B) + (uint32_t)C::TILE_BYTES;
   const int lb = p.blk_log2;
   const long long cbm = (1LL << lb) - 1;
+  // addresses: per-thread bases plus compile-time offsets (epi_addr.cuh)
+  using A2s = typename Conv2dColAddr<C>::template E2<0>;
+  using A2h = typename Conv2dColAddr<C>::template E2<1>;
+  using A4q = typename Conv2dColAddr<C>::template E4<0>;
+  using A4r = typename Conv2dColAddr<C>::template E4<1>;
+  constexpr int kW0 = 2 + C::kEpiWarps;
+  constexpr int kK2s = C::kColPairs2 ? epi::addr_kind<A2s, kW0, C::kEpiWarps, G2g::BPW, G2g::CH, 8, 2>() : 0;
+  constexpr int kK2h = C::kColPairs2 ? epi::addr_kind<A2h, kW0, C::kEpiWarps, G2g::BPW, G2g::CH, 8, 2>() : 0;
+  constexpr int kK4q = epi::addr_kind<A4q, kW0, C::kEpiWarps, G4g::BPW, G4g::CH, 8, 2>();
+  constexpr int kK4r = epi::addr_kind<A4r, kW0, C::kEpiWarps, G4g::BPW, G4g::CH, 8, 2>();
+  uint32_t base2s[G2g::BPW][kK2s == 1 ? 4 : 1], base2h[G2g::BPW][kK2h == 1 ? 4 : 1];
+  uint32_t base4q[G4g::BPW][kK4q == 1 ? 4 : 1], base4r[G4g::BPW][kK4r == 1 ? 4 : 1];
+#pragma unroll
+  for (int bi = 0; bi < G2g::BPW; ++bi)
+#pragma unroll
+    for (int jh = 0; jh < 4; ++jh) {
+      if (jh < (kK2s == 1 ? 4 : 1)) base2s[bi][kK2s == 1 ? jh : 0] = b3 + A2s::f((int)warp, (int)lane, bi, 0, 2 * jh);
+      if (jh < (kK2h == 1 ? 4 : 1)) base2h[bi][kK2h == 1 ? jh : 0] = A2h::f((int)warp, (int)lane, bi, 0, 2 * jh);
+    }
+#pragma unroll
+  for (int bi = 0; bi < G4g::BPW; ++bi)
+#pragma unroll
+    for (int jh = 0; jh < 4; ++jh) {
+      if (jh < (kK4q == 1 ? 4 : 1)) base4q[bi][kK4q == 1 ? jh : 0] = A4q::f((int)warp, (int)lane, bi, 0, 2 * jh);
+      if (jh < (kK4r == 1 ? 4 : 1)) base4r[bi][kK4r == 1 ? jh : 0] = A4r::f((int)warp, (int)lane, bi, 0, 2 * jh);
+    }
+  const uint32_t rows4 = (uint32_t)p.rows * 4u;
 
   for (int r = 1; r < ntiles + 3; ++r) {
     // ---------------------------------------------------------------- E2(r-1)
@@ -302,19 +451,28 @@ __device__ __forceinline__ void conv2d_cols_group_b(const FftParams& p, int ntil
       if (!mbar_wait_warp(&sh.h_full[hs], (uint32_t)(j2 / C::HS) & 1u, p.err, kDevTimeoutEpilogue)) return;
       tc_fence_after();
       const uint32_t hbase = smem_u32(sh.smem + C::OFF_H + hs * C::SPEC_BYTES);
+      // 32-column TMEM pieces, the next one loading while this one is processed
+      constexpr int kNIT2 = G2g::BPW * G2g::CH * 2;
+      auto taddr2 = [&](int it) -> uint32_t {
+        const int bi = it / (2 * G2g::CH), c = (it / 2) % G2g::CH, hh = it & 1;
+        return tmem + (G2g::lanes(q, h, bi, C::lane_off(C::M2, 0)) << 16) + C::col_off(C::M2, 1, 0) + (uint32_t)(ch02 + c) * 64u + 32u * (uint32_t)hh;
+      };
+      uint32_t vb[2][16];
+      tmem_ld_16x256b_x4(taddr2(0), vb[0]);
 #pragma unroll
       for (int bi = 0; bi < G2g::BPW; ++bi) {
         const int rp = G2g::block(q, h, bi) * 8 + (int)(lane >> 2);
         const int g2 = rp / C::NA, ka = rp % C::NA;
         const uint32_t krow = (uint32_t)detail::stage2_krow(C::R2, g2 * C::NA + ka);
-        const uint32_t base = tmem + (G2g::lanes(q, h, bi, C::lane_off(C::M2, 0)) << 16) + C::col_off(C::M2, 1, 0);
 #pragma unroll
         for (int c = 0; c < G2g::CH; ++c) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {   // two 32-column loads: 16 registers in flight
-          uint32_t v[16];
-          tmem_ld_16x256b_x4(base + (uint32_t)(ch02 + c) * 64u + 32u * (uint32_t)hh, v);
+          const int it = (bi * G2g::CH + c) * 2 + hh;
           tmem_wait_ld();
+          tmem_regs_ready(vb[it & 1]);
+          if (it + 1 < kNIT2) tmem_ld_16x256b_x4(taddr2(it + 1), vb[(it + 1) & 1]);
+          const uint32_t (&v)[16] = vb[it & 1];
           if constexpr (C::kColPairs2) {
             // iterations j, j + 1 hold ks0 = 8m + 2 l4 and ks0 + 1 of one signal
 #pragma unroll
@@ -333,20 +491,31 @@ __device__ __forceinline__ void conv2d_cols_group_b(const FftParams& p, int ntil
                 xr[e] = RR - II;
                 xi[e] = IR + RI;
               }
-              const uint32_t byte = (uint32_t)(sl * C::N + k0) * 8u;
-              float4 w = ld_shared_v4f(hbase + (byte ^ (((byte >> 7) & 7u) << 4)));
+              uint32_t sbyte;
+              if constexpr (kK2h != 0) {
+                sbyte = base2h[bi][kK2h == 1 ? jj / 2 : 0] + epi::addr_delta<A2h, kW0, kK2h>(bi, c, jj);
+              } else {
+                const uint32_t byte = (uint32_t)(sl * C::N + k0) * 8u;
+                sbyte = byte ^ (((byte >> 7) & 7u) << 4);
+              }
+              float4 w = ld_shared_v4f(hbase + sbyte);
               w.x *= sc2; w.y *= sc2; w.z *= sc2; w.w *= sc2;
               const float z0r = xr[0] * w.x - xi[0] * w.y, z0i = xr[0] * w.y + xi[0] * w.x;
               const float z1r = xr[1] * w.z - xi[1] * w.w, z1i = xr[1] * w.w + xi[1] * w.z;
-              const int col = c2 * 2 * C::NS + 2 * ks0;
-              const uint32_t off = (uint32_t)(col / C::E) * C::LBO2 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
+              uint32_t addr;
+              if constexpr (kK2s != 0) {
+                addr = base2s[bi][kK2s == 1 ? jj / 2 : 0] + epi::addr_delta<A2s, kW0, kK2s>(bi, c, jj);
+              } else {
+                const int col = c2 * 2 * C::NS + 2 * ks0;
+                addr = b3 + (uint32_t)(col / C::E) * C::LBO2 + D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
+              }
               if constexpr (C::kIsHalf) {
                 __half2 h0 = __floats2half2_rn(z0r, z0i), h1 = __floats2half2_rn(z1r, z1i);
-                asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(b3 + off), "r"(*reinterpret_cast<uint32_t*>(&h0)),
+                asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(*reinterpret_cast<uint32_t*>(&h0)),
                              "r"(*reinterpret_cast<uint32_t*>(&h1))
                              : "memory");
               } else {
-                st_shared_v4(b3 + off, __float_as_uint(round_tf32(z0r)), __float_as_uint(round_tf32(z0i)),
+                st_shared_v4(addr, __float_as_uint(round_tf32(z0r)), __float_as_uint(round_tf32(z0i)),
                              __float_as_uint(round_tf32(z1r)), __float_as_uint(round_tf32(z1i)));
               }
             }
@@ -386,18 +555,29 @@ __device__ __forceinline__ void conv2d_cols_group_b(const FftParams& p, int ntil
       const long long tile = blockIdx.x + (long long)j4 * gridDim.x;
       const long long sig0 = tile * C::T;
       const long long img = sig0 / p.rows, r0 = sig0 - img * p.rows;
+      // element base of this tile in the block-width-4 layout: img N rows + r0 * 4
+      uint8_t* const tile_out = reinterpret_cast<uint8_t*>(p.out) + (img * C::N * p.rows + r0 * 4) * (C::kIsHalf ? 4 : 8);
+      // 32-column TMEM pieces, the next one loading while this one is processed
+      constexpr int kNIT4 = G4g::BPW * G4g::CH * 2;
+      auto taddr4 = [&](int it) -> uint32_t {
+        const int bi = it / (2 * G4g::CH), c = (it / 2) % G4g::CH, hh = it & 1;
+        return tmem + (G4g::lanes(q, h, bi, C::lane_off(C::M1, 1)) << 16) + C::col_off(C::M1, 0, 1) + (uint32_t)(ch04 + c) * 64u + 32u * (uint32_t)hh;
+      };
+      uint32_t vb[2][16];
+      tmem_ld_16x256b_x4(taddr4(0), vb[0]);
 #pragma unroll
       for (int bi = 0; bi < G4g::BPW; ++bi) {
         const int rp = G4g::block(q, h, bi) * 8 + (int)(lane >> 2);
         const int g4 = rp / C::NS, kap = rp % C::NS;
-        const uint32_t base = tmem + (G4g::lanes(q, h, bi, C::lane_off(C::M1, 1)) << 16) + C::col_off(C::M1, 0, 1);
 #pragma unroll
         for (int c = 0; c < G4g::CH; ++c) {
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {   // two 32-column loads: 16 registers in flight
-          uint32_t v[16];
-          tmem_ld_16x256b_x4(base + (uint32_t)(ch04 + c) * 64u + 32u * (uint32_t)hh, v);
+          const int it = (bi * G4g::CH + c) * 2 + hh;
           tmem_wait_ld();
+          tmem_regs_ready(vb[it & 1]);
+          if (it + 1 < kNIT4) tmem_ld_16x256b_x4(taddr4(it + 1), vb[(it + 1) & 1]);
+          const uint32_t (&v)[16] = vb[it & 1];
 #pragma unroll
           for (int j2 = 0; j2 < 4; j2 += 2) {
             const int jj = 4 * hh + j2;
@@ -417,6 +597,23 @@ __device__ __forceinline__ void conv2d_cols_group_b(const FftParams& p, int ntil
             }
             // column-blocked [img][m / Cb][column][m % Cb]; m0 even, so with
             // Cb >= 2 outputs m0 and m0 + 1 are neighbours
+            if (lb == 2) {
+              // Cb = 4: ((img N + m0) >> 2) rows 4 + (r0 + sl) 4 + (m0 & 3), N a multiple of 4
+              uint32_t mq, er;
+              if constexpr (kK4q != 0) mq = base4q[bi][kK4q == 1 ? jj / 2 : 0] + epi::addr_delta<A4q, kW0, kK4q>(bi, c, jj);
+              else mq = A4q::f((int)warp, (int)lane, bi, c, jj);
+              if constexpr (kK4r != 0) er = base4r[bi][kK4r == 1 ? jj / 2 : 0] + epi::addr_delta<A4r, kW0, kK4r>(bi, c, jj);
+              else er = A4r::f((int)warp, (int)lane, bi, c, jj);
+              const uint32_t e = mq * rows4 + er;
+              if constexpr (C::kIsHalf) {
+                __half2 h0 = __floats2half2_rn(xr[0], xi[0]), h1 = __floats2half2_rn(xr[1], xi[1]);
+                *reinterpret_cast<uint2*>(reinterpret_cast<uint32_t*>(tile_out) + e) =
+                    make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+              } else {
+                *reinterpret_cast<float4*>(reinterpret_cast<float2*>(tile_out) + e) = make_float4(xr[0], xi[0], xr[1], xi[1]);
+              }
+              continue;
+            }
             const long long o0 = (((img * C::N + m0) >> lb) * p.rows + r0 + sl) * (cbm + 1) + (m0 & cbm);
             if (lb >= 1) {
               if constexpr (C::kIsHalf) {

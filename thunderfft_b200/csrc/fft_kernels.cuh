@@ -38,6 +38,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 #include "sm100.cuh"
+#include "epi_addr.cuh"
 
 namespace thff {
 
@@ -304,6 +305,97 @@ __device__ __forceinline__ uint32_t in_tile_offset(int sig, int s, int a) {
   return atom * C::LBO1 + C::D::swz(krow * 128u + e * C::ESZ);
 }
 
+// Stage-1 epilogue geometry of fft2_kernel (one accumulator per stage): M=64
+// -> one 16-row block per TMEM lane quadrant, its 64-column chunks split over
+// the EPW warps of the quadrant; M=128 -> two row blocks per quadrant, split
+// over the EPW warps.
+template <int kM, int kNcols, int kEPW>
+struct EpiGeo {
+  static constexpr int kNC = kNcols / 64;
+  static constexpr int BPW = (kM == 64) ? 1 : 2 / kEPW;
+  static constexpr int CH = (kM == 64) ? kNC / kEPW : kNC;
+  __host__ __device__ static constexpr int ch0(int h) { return (kM == 64 && kEPW > 1) ? h * CH : 0; }
+  __host__ __device__ static constexpr int block(int q, int h, int bi) { return (kM == 64) ? q : 2 * q + h * BPW + bi; }
+};
+
+// Byte offset in the stage-2 operand buffer of the value that stage-1
+// epilogue warp `warp` (absolute index), lane `lane` writes for row block bi,
+// chunk c and output o (input modes with one chunk per signal group).
+template <class C, int kIn, bool kColPairs>
+struct Fft2E1Off {
+  __host__ __device__ static constexpr uint32_t f(int warp, int lane, int bi, int c, int o) {
+    using G = EpiGeo<C::M1, C::N1, C::EPW>;
+    const int q = warp & 3, h = (warp - 2) >> 2, l = lane & 3;
+    const int ch0 = G::ch0(h);
+    const int rp = G::block(q, h, bi) * 8 + (lane >> 2);
+    const int g1 = rp / C::NS, ks = rp % C::NS;
+    int c1 = 0, a = 0;
+    if (kIn == kInPairPlanar) {
+      const int jr = (C::NA == 16) ? ((o >> 1) >> 1) * 4 + ((o >> 1) & 1) : (o >> 1);
+      const int col = 64 * (ch0 + c) + 8 * jr + 2 * l + (o & 1);
+      c1 = col / (2 * C::NA);
+      a = col % (2 * C::NA);
+    } else {
+      const int pidx = 4 * ((ch0 + c) * 8 + o) + l;
+      if (kIn == kInNatural) { c1 = pidx / C::NA; a = pidx % C::NA; }
+      else { a = pidx / C::C1; c1 = pidx % C::C1; }
+    }
+    const int sig = g1 * C::C1 + c1;
+    const int g2 = sig / C::C2, c2 = sig % C::C2;
+    const uint32_t krow = (uint32_t)stage2_krow(stage2_rotation(C::kIsHalf, C::kVariant), g2 * C::NA + a);
+    const int col = c2 * 2 * C::NS + 2 * (kColPairs ? stage2_col_pair(ks) : ks);
+    return (uint32_t)(col / C::E) * C::LBO2 + C::D::swz(krow * 128u + (uint32_t)(col % C::E) * C::ESZ);
+  }
+};
+
+// Stage-2 epilogue with column pairs: the outputs k0, k0 + 1 of tile signal
+// sl that warp `warp`, lane `lane` holds for row block bi, chunk c and
+// iteration pair j (even).  kWhat 0: sl * N + k0 (element offset in the
+// tile's natural output rows); 1: sl; 2: the 128-B-swizzled byte offset of
+// that element in a staged complex fp32 tile.
+template <class C, int kWhat>
+struct Fft2E2Pos {
+  __host__ __device__ static constexpr uint32_t f(int warp, int lane, int bi, int c, int j) {
+    using G = EpiGeo<C::M2, C::N2, C::EPW>;
+    const int q = warp & 3, h = (warp - 2 - C::kEpiWarps) >> 2, l4 = lane & 3;
+    const int rp = G::block(q, h, bi) * 8 + (lane >> 2);
+    const int g2 = rp / C::NA, ka = rp % C::NA;
+    const int pidx = 4 * ((G::ch0(h) + c) * 8 + j) + l4;
+    const int c2 = pidx / C::NS, pp = pidx % C::NS;
+    const int k0 = C::NS * ka + (pp & ~7) + 2 * l4;
+    const int sl = g2 * C::C2 + c2;
+    if (kWhat == 1) return (uint32_t)sl;
+    const uint32_t e = (uint32_t)(sl * C::N + k0);
+    if (kWhat == 0) return e;
+    const uint32_t byte = e * 8u;
+    return byte ^ (((byte >> 7) & 7u) << 4);
+  }
+};
+
+// Stage-2 epilogue, half2 column-blocked output with block width 4 and
+// paired signal rows: for the jv-th stored iteration j of chunk c (the j with
+// (j / PJ) even, PJ = NS / 4), kWhat 0: k >> 2 (the output's block row),
+// 1: the element offset inside the block rows, (sl + row) * 4 + 2 (l4 & 1),
+// where row 0/1 is the signal row this lane stores.  The element offset of
+// the store is then (k >> 2) * rows * 4 + kWhat-1 value + the tile's base.
+template <class C, int kWhat>
+struct Fft2E2PairRows {
+  __host__ __device__ static constexpr uint32_t f(int warp, int lane, int bi, int c, int jv) {
+    using G = EpiGeo<C::M2, C::N2, C::EPW>;
+    constexpr int PJ = C::NS / 4;
+    const int j = (jv / PJ) * 2 * PJ + (jv % PJ);
+    const int q = warp & 3, h = (warp - 2 - C::kEpiWarps) >> 2, l4 = lane & 3;
+    const int rp = G::block(q, h, bi) * 8 + (lane >> 2);
+    const int g2 = rp / C::NA, ka = rp % C::NA;
+    const int pidx = 4 * ((G::ch0(h) + c) * 8 + j) + l4;
+    const int c2 = pidx / C::NS, ks = pidx % C::NS;
+    const int sl = g2 * C::C2 + c2;
+    const int k = C::NS * ka + ks;
+    if (kWhat == 0) return (uint32_t)(k >> 2);
+    return (uint32_t)((sl + (l4 < 2 ? 0 : 1)) * 4 + 2 * (l4 & 1));
+  }
+};
+
 }  // namespace detail
 
 // ---------------------------------------------------------------------------
@@ -569,6 +661,15 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
       }
     }
     const uint32_t ybase = smem_u32(smem + C::OFF_Y);
+    // store addresses: per-thread bases plus compile-time offsets (epi_addr.cuh)
+    using E1Off = detail::Fft2E1Off<C, kIn, kColPairs>;
+    constexpr int kAK = (GC == 1) ? epi::addr_kind<E1Off, 2, C::kEpiWarps, BPW, CH, 8>() : 0;
+    uint32_t abase[BPW][kAK == 1 ? 8 : 1];
+#pragma unroll
+    for (int bi = 0; bi < BPW; ++bi) {
+#pragma unroll
+      for (int o = 0; o < (kAK == 1 ? 8 : 1); ++o) abase[bi][o] = E1Off::f((int)warp, (int)lane, bi, 0, o);
+    }
     for (int i = 0; i < my_tiles; ++i) {
       const int buf = i & 1;
       const uint32_t ph = (uint32_t)(i >> 1) & 1u;
@@ -576,55 +677,90 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
       if (!mbar_wait_warp(&bar_y_empty[buf], ph ^ 1u, p.err, kDevTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t yb = ybase + buf * C::TILE_BYTES;
-#pragma unroll
-      for (int bi = 0; bi < BPW; ++bi) {
+      // One output: the four partial sums cos*re, cos*im, sin*re, sin*im of
+      // stage-1 output (ks, a) -> twiddled complex value into the stage-2 operand.
+      auto emit1 = [&](int bi, int c, int o, float rr, float ri, float ir, float ii) {
         const int block = (C::M1 == 64) ? (int)q : (int)(2 * q) + h * BPW + bi;
-        const uint32_t lanes = (C::M1 == 64) ? 32u * q + 16u * buf : 32u * q + 16u * (uint32_t)(h * BPW + bi);
-        const uint32_t cols = (C::M1 == 64) ? 0u : (uint32_t)(buf * C::N1);
         const int rp = block * 8 + (int)(lane >> 2);
         const int g1 = rp / C::NS, ks = rp % C::NS;
+        int c1, a, slot;
+        if constexpr (kIn == kInPairPlanar) {
+          constexpr int d = C::NA / 8;  // sub-chunks between the re and im planes
+          const int jr = (C::NA == 16) ? ((o >> 1) >> 1) * 4 + ((o >> 1) & 1) : (o >> 1);
+          const int e = o & 1;
+          const int col = 64 * (ch0 + c) + 8 * jr + 2 * l + e;
+          c1 = col / (2 * C::NA); a = col % (2 * C::NA);
+          slot = 2 * (jr % d) + e;
+        } else {
+          const int pidx = 4 * ((ch0 + c) * 8 + o) + l;
+          if constexpr (kIn == kInNatural) {
+            c1 = pidx / C::NA; a = pidx % C::NA;
+            // a = l + 4*((ch0+c)*8 + o) mod NA -> slot ((ch0+c)*8 + o) mod NA/4
+            // = (c*8 + o) mod NA/4 because ch0*8 is a multiple of NA/4
+            slot = (c * 8 + o) % kTw;
+          } else {
+            a = pidx / C::C1; c1 = pidx % C::C1;
+            slot = (c * 8 + o) / kTq;
+          }
+        }
+        const float yr = rr - ii, yi = ir + ri;
+        const float2 w = tw[bi][slot];
+        const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
+        uint32_t off;
+        if constexpr (kAK != 0) {
+          off = abase[bi][kAK == 1 ? o : 0] + epi::addr_delta<E1Off, 2, kAK>(bi, c, o);
+        } else {
+          const int sig = g1 * C::C1 + c1;
+          const int g2 = sig / C::C2, c2 = sig % C::C2;
+          const uint32_t krow = (uint32_t)detail::stage2_krow(detail::stage2_rotation(C::kIsHalf, C::kVariant), g2 * C::NA + a);
+          const int col = c2 * 2 * C::NS + 2 * (kColPairs ? detail::stage2_col_pair(ks) : ks);
+          off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
+        }
+        detail::store_complex<C::kIsHalf>(yb + off, zr, zi);
+      };
+      // TMEM address of (row block bi, chunk c) of this tile's accumulator
+      auto acc1 = [&](int bi, int c) -> uint32_t {
+        const uint32_t lanes = (C::M1 == 64) ? 32u * q + 16u * buf : 32u * q + 16u * (uint32_t)(h * BPW + bi);
+        const uint32_t cols = (C::M1 == 64) ? 0u : (uint32_t)(buf * C::N1);
+        return tmem + (lanes << 16) + cols + (uint32_t)(ch0 + c) * 64u;
+      };
+      if constexpr (kIn != kInPairPlanar) {
+        // 32-column pieces, the next one loading while this one is processed
+        constexpr int NIT = BPW * CH * 2;
+        uint32_t rb[2][16];
+        tmem_ld_16x256b_x4(acc1(0, 0), rb[0]);
 #pragma unroll
-        for (int c = 0; c < CH; c += GC) {
-          uint32_t r[GC][32];
-#pragma unroll
-          for (int g = 0; g < GC; ++g) tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c + g) * 64, r[g]);
+        for (int it = 0; it < NIT; ++it) {
           tmem_wait_ld();
+          tmem_regs_ready(rb[it & 1]);
+          if (it + 1 < NIT)
+            tmem_ld_16x256b_x4(acc1((it + 1) / (2 * CH), ((it + 1) / 2) % CH) + 32u * (uint32_t)((it + 1) & 1),
+                               rb[(it + 1) & 1]);
+          const int bi = it / (2 * CH), c = (it / 2) % CH, hh = it & 1;
 #pragma unroll
-          for (int o = 0; o < 8 * GC; ++o) {
-            // registers of cos*re, cos*im, sin*re, sin*im of this output; (c1, a); twiddle slot
-            int iRR, iRI, iIR, iII, c1, a, slot;
-            if constexpr (kIn == kInPairPlanar) {
+          for (int oo = 0; oo < 4; ++oo)
+            emit1(bi, c, 4 * hh + oo, __uint_as_float(rb[it & 1][4 * oo]), __uint_as_float(rb[it & 1][4 * oo + 1]),
+                  __uint_as_float(rb[it & 1][4 * oo + 2]), __uint_as_float(rb[it & 1][4 * oo + 3]));
+        }
+      } else {
+#pragma unroll
+        for (int bi = 0; bi < BPW; ++bi) {
+#pragma unroll
+          for (int c = 0; c < CH; c += GC) {
+            uint32_t r[GC][32];
+#pragma unroll
+            for (int g = 0; g < GC; ++g) tmem_ld_16x256b_x8(acc1(bi, c + g), r[g]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int o = 0; o < 8 * GC; ++o) {
+              // registers of cos*re, cos*im, sin*re, sin*im of this output
               constexpr int d = C::NA / 8;  // sub-chunks between the re and im planes
               const int jr = (C::NA == 16) ? ((o >> 1) >> 1) * 4 + ((o >> 1) & 1) : (o >> 1);
               const int e = o & 1;
-              iRR = 4 * jr + e; iIR = 4 * jr + 2 + e; iRI = 4 * (jr + d) + e; iII = 4 * (jr + d) + 2 + e;
-              const int col = 64 * (ch0 + c) + 8 * jr + 2 * l + e;
-              c1 = col / (2 * C::NA); a = col % (2 * C::NA);
-              slot = 2 * (jr % d) + e;
-            } else {
-              iRR = 4 * o; iRI = 4 * o + 1; iIR = 4 * o + 2; iII = 4 * o + 3;
-              const int pidx = 4 * ((ch0 + c) * 8 + o) + l;
-              if constexpr (kIn == kInNatural) {
-                c1 = pidx / C::NA; a = pidx % C::NA;
-                // a = l + 4*((ch0+c)*8 + o) mod NA -> slot ((ch0+c)*8 + o) mod NA/4
-                // = (c*8 + o) mod NA/4 because ch0*8 is a multiple of NA/4
-                slot = (c * 8 + o) % kTw;
-              } else {
-                a = pidx / C::C1; c1 = pidx % C::C1;
-                slot = (c * 8 + o) / kTq;
-              }
+              const int iRR = 4 * jr + e, iIR = 4 * jr + 2 + e, iRI = 4 * (jr + d) + e, iII = 4 * (jr + d) + 2 + e;
+              emit1(bi, c, o, __uint_as_float(r[iRR >> 5][iRR & 31]), __uint_as_float(r[iRI >> 5][iRI & 31]),
+                    __uint_as_float(r[iIR >> 5][iIR & 31]), __uint_as_float(r[iII >> 5][iII & 31]));
             }
-            const float rr = __uint_as_float(r[iRR >> 5][iRR & 31]), ri = __uint_as_float(r[iRI >> 5][iRI & 31]);
-            const float ir = __uint_as_float(r[iIR >> 5][iIR & 31]), ii = __uint_as_float(r[iII >> 5][iII & 31]);
-            const float yr = rr - ii, yi = ir + ri;
-            const float2 w = tw[bi][slot];
-            const int sig = g1 * C::C1 + c1;
-            const int g2 = sig / C::C2, c2 = sig % C::C2;
-            const uint32_t krow = (uint32_t)detail::stage2_krow(detail::stage2_rotation(C::kIsHalf, C::kVariant), g2 * C::NA + a);
-            const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
-            const int col = c2 * 2 * C::NS + 2 * (kColPairs ? detail::stage2_col_pair(ks) : ks);
-            const uint32_t off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
-            detail::store_complex<C::kIsHalf>(yb + off, zr, zi);
           }
         }
       }
@@ -641,10 +777,40 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
     constexpr int BPW = (C::M2 == 64) ? 1 : 2 / C::EPW;
     constexpr int CH = (C::M2 == 64) ? kNC / C::EPW : kNC;
     const int ch0 = (C::M2 == 64 && C::EPW > 1) ? h * CH : 0;
+    // column-pair outputs: per-thread bases of the element offset, the signal
+    // and the staged-spectrum byte offset (epi_addr.cuh)
+    constexpr int kE2W0 = 2 + C::kEpiWarps;
+    using PosOff = detail::Fft2E2Pos<C, 0>;
+    using SigOff = detail::Fft2E2Pos<C, 1>;
+    using SpecOff = detail::Fft2E2Pos<C, 2>;
+    constexpr int kPosK = kColPairs ? epi::addr_kind<PosOff, kE2W0, C::kEpiWarps, BPW, CH, 8, 2>() : 0;
+    constexpr int kSigK = kColPairs ? epi::addr_kind<SigOff, kE2W0, C::kEpiWarps, BPW, CH, 8, 2>() : 0;
+    constexpr int kSpecK = (kColPairs && kStageH) ? epi::addr_kind<SpecOff, kE2W0, C::kEpiWarps, BPW, CH, 8, 2>() : 0;
+    uint32_t pos_base[BPW][kPosK == 1 ? 4 : 1], sig_base[BPW][kSigK == 1 ? 4 : 1], spec_base[BPW][kSpecK == 1 ? 4 : 1];
+    // half2 column-blocked output with paired signal rows (block width 4)
+    constexpr bool kPairRows = kEpi == kEpiBlocked && kOutHalf && C::NS <= 16 && C::C2 % 2 == 0;
+    using KqOff = detail::Fft2E2PairRows<C, 0>;
+    using ErOff = detail::Fft2E2PairRows<C, 1>;
+    constexpr int kKqK = kPairRows ? epi::addr_kind<KqOff, kE2W0, C::kEpiWarps, BPW, CH, 4>() : 0;
+    constexpr int kErK = kPairRows ? epi::addr_kind<ErOff, kE2W0, C::kEpiWarps, BPW, CH, 4>() : 0;
+    uint32_t kq_base[BPW][kKqK == 1 ? 4 : 1], er_base[BPW][kErK == 1 ? 4 : 1];
+    const uint32_t rows4 = (uint32_t)p.rows * 4u;
+#pragma unroll
+    for (int bi = 0; bi < BPW; ++bi) {
+#pragma unroll
+      for (int jh = 0; jh < 4; ++jh) {
+        if (jh < (kPosK == 1 ? 4 : 1)) pos_base[bi][kPosK == 1 ? jh : 0] = PosOff::f((int)warp, (int)lane, bi, 0, 2 * jh);
+        if (jh < (kSigK == 1 ? 4 : 1)) sig_base[bi][kSigK == 1 ? jh : 0] = SigOff::f((int)warp, (int)lane, bi, 0, 2 * jh);
+        if (jh < (kSpecK == 1 ? 4 : 1)) spec_base[bi][kSpecK == 1 ? jh : 0] = SpecOff::f((int)warp, (int)lane, bi, 0, 2 * jh);
+        if (jh < (kKqK == 1 ? 4 : 1)) kq_base[bi][kKqK == 1 ? jh : 0] = KqOff::f((int)warp, (int)lane, bi, 0, jh);
+        if (jh < (kErK == 1 ? 4 : 1)) er_base[bi][kErK == 1 ? jh : 0] = ErOff::f((int)warp, (int)lane, bi, 0, jh);
+      }
+    }
     for (int i = 0; i < my_tiles; ++i) {
       const long long tile = blockIdx.x + (long long)i * gridDim.x;
       const int buf = i & 1;
       const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+      const bool full_tile = (tile + 1) * C::T <= batch;   // no per-output bounds test
       if (!mbar_wait_warp(&bar_acc2_full[buf], ph, p.err, kDevTimeoutEpilogue)) break;
       const int hs = kStageH ? i % (C::HS > 0 ? C::HS : 1) : 0;
       if constexpr (kStageH)
@@ -696,58 +862,69 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
           // and k0 + 1 of one signal (stage2_col_pair)
           constexpr int kVec = kOutHalf ? 8 : 16;   // bytes of two complex outputs
           const bool vec_ok = kEpi != kEpiNatural || (reinterpret_cast<uintptr_t>(p.out) & (kVec - 1)) == 0;
+          // 32-column pieces, the next one loading while this one is processed
+          constexpr int NIT2 = CH * 2;
+          uint32_t rb[2][16];
+          tmem_ld_16x256b_x4(tmem + (lanes << 16) + cols + (uint32_t)ch0 * 64u, rb[0]);
 #pragma unroll
-          for (int c = 0; c < CH; ++c) {
-            uint32_t r[32];
-            tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (ch0 + c) * 64, r);
+          for (int it = 0; it < NIT2; ++it) {
             tmem_wait_ld();
+            tmem_regs_ready(rb[it & 1]);
+            if (it + 1 < NIT2)
+              tmem_ld_16x256b_x4(tmem + (lanes << 16) + cols + (uint32_t)(ch0 + (it + 1) / 2) * 64u + 32u * (uint32_t)((it + 1) & 1),
+                                 rb[(it + 1) & 1]);
+            const int c = it / 2;
+            const uint32_t (&r)[16] = rb[it & 1];
 #pragma unroll
-            for (int j = 0; j < 8; j += 2) {
-              const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)(lane & 3u);
-              const int c2 = pidx / C::NS, pp = pidx % C::NS;     // pp = 8m + l
-              const int k0 = C::NS * ka + (pp & ~7) + 2 * (int)(lane & 3u);
-              const int sl = g2 * C::C2 + c2;
+            for (int j = 4 * (it & 1); j < 4 * (it & 1) + 4; j += 2) {
+              // element offset sl * N + k0 and signal sl from per-thread bases
+              // (epi_addr.cuh; the generic forms otherwise)
+              uint32_t pos, sl_u, sbyte = 0u;
+              if constexpr (kPosK != 0) pos = pos_base[bi][kPosK == 1 ? j / 2 : 0] + epi::addr_delta<PosOff, kE2W0, kPosK>(bi, c, j);
+              else pos = PosOff::f((int)warp, (int)lane, bi, c, j);
+              if constexpr (kSigK != 0) sl_u = sig_base[bi][kSigK == 1 ? j / 2 : 0] + epi::addr_delta<SigOff, kE2W0, kSigK>(bi, c, j);
+              else sl_u = SigOff::f((int)warp, (int)lane, bi, c, j);
+              if constexpr (kStageH) {
+                if constexpr (kSpecK != 0) sbyte = spec_base[bi][kSpecK == 1 ? j / 2 : 0] + epi::addr_delta<SpecOff, kE2W0, kSpecK>(bi, c, j);
+                else sbyte = SpecOff::f((int)warp, (int)lane, bi, c, j);
+              }
+              const int sl = (int)sl_u;
               float xr[2], xi[2];
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const int jj = j + e;
-                const float rr = __uint_as_float(r[4 * jj + 0]), ri = __uint_as_float(r[4 * jj + 1]);
-                const float ir = __uint_as_float(r[4 * jj + 2]), ii = __uint_as_float(r[4 * jj + 3]);
+                const int jl = (j + e) & 3;   // register group within the 32-column piece
+                const float rr = __uint_as_float(r[4 * jl + 0]), ri = __uint_as_float(r[4 * jl + 1]);
+                const float ir = __uint_as_float(r[4 * jl + 2]), ii = __uint_as_float(r[4 * jl + 3]);
                 xr[e] = rr - ii;
                 xi[e] = ir + ri;
               }
-              if (sig0 + sl < batch) {
+              if (full_tile || sig0 + sl < batch) {
                 if constexpr (kEpi == kEpiUnpackPair) {
                   // fp32 real outputs: Re -> image b, Im -> image b + 1
-                  *reinterpret_cast<float2*>(y0 + sl * C::N + k0) =
-                      make_float2(xr[0] * osc * osc2, xr[1] * osc * osc2);
-                  if (y1)
-                    *reinterpret_cast<float2*>(y1 + sl * C::N + k0) =
-                        make_float2(xi[0] * osc * osc2, xi[1] * osc * osc2);
+                  *reinterpret_cast<float2*>(y0 + pos) = make_float2(xr[0] * osc * osc2, xr[1] * osc * osc2);
+                  if (y1) *reinterpret_cast<float2*>(y1 + pos) = make_float2(xi[0] * osc * osc2, xi[1] * osc * osc2);
                 } else {
                   if constexpr (kEpi == kEpiMulNatural) {
                     // spectrum values at k0 (x, y) and k0 + 1 (z, w): one 16-B piece
                     float4 w;
                     if constexpr (kStageH) {
-                      const uint32_t byte = (uint32_t)(sl * C::N + k0) * 8u;
-                      w = ld_shared_v4f(hbase + (byte ^ (((byte >> 7) & 7u) << 4)));
+                      w = ld_shared_v4f(hbase + sbyte);
                     } else {
-                      w = __ldg(reinterpret_cast<const float4*>(spec_t + sl * C::N + k0));
+                      w = __ldg(reinterpret_cast<const float4*>(spec_t + pos));
                     }
                     w.x *= osc; w.y *= osc; w.z *= osc; w.w *= osc;
                     const float a0 = xr[0] * w.x - xi[0] * w.y, b0 = xr[0] * w.y + xi[0] * w.x;
                     const float a1 = xr[1] * w.z - xi[1] * w.w, b1 = xr[1] * w.w + xi[1] * w.z;
                     xr[0] = a0; xi[0] = b0; xr[1] = a1; xi[1] = b1;
                   }
-                  const long long o = (sig0 + sl) * C::N + k0;
                   if constexpr (kOutHalf) {
                     __half2 h0 = __floats2half2_rn(xr[0], xi[0]), h1 = __floats2half2_rn(xr[1], xi[1]);
-                    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + o;
+                    uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + sig0 * C::N + pos;
                     const uint32_t v0 = *reinterpret_cast<uint32_t*>(&h0), v1 = *reinterpret_cast<uint32_t*>(&h1);
                     if (vec_ok) *reinterpret_cast<uint2*>(dst) = make_uint2(v0, v1);
                     else { dst[0] = v0; dst[1] = v1; }   // output only 4-byte aligned
                   } else {
-                    float2* dst = reinterpret_cast<float2*>(p.out) + o;
+                    float2* dst = reinterpret_cast<float2*>(p.out) + sig0 * C::N + pos;
                     if (vec_ok) *reinterpret_cast<float4*>(dst) = make_float4(xr[0], xi[0], xr[1], xi[1]);
                     else { dst[0] = make_float2(xr[0], xi[0]); dst[1] = make_float2(xr[1], xi[1]); }
                   }
@@ -761,8 +938,9 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
         // and a thread holds both (iterations j and j + NS/4).  Two quad
         // shuffles per value let each lane store 8 bytes, so one store
         // instruction writes whole 32-byte sectors.
-        constexpr bool kPairRows = kEpi == kEpiBlocked && kOutHalf && C::NS <= 16 && C::C2 % 2 == 0;
         const bool pair_rows = kPairRows && p.blk_log2 == 2;
+        // tile base of the paired-row blocked output: img N rows + r0 * 4 elements
+        uint32_t* const blk_out = reinterpret_cast<uint32_t*>(p.out) + (img * C::N * p.rows + r0 * 4);
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
           uint32_t r[32];
@@ -775,10 +953,14 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
                 if ((j / PJ) % 2 != 0) continue;
-                const int pidx = 4 * ((ch0 + c) * 8 + j) + (int)l4;
-                const int c2 = pidx / C::NS, ks = pidx % C::NS;   // c2 even: rows sl, sl + 1
-                const int sl = g2 * C::C2 + c2;
-                const int k = C::NS * ka + ks;
+                const int jv = (j / (2 * PJ)) * PJ + j % PJ;
+                // block row k >> 2 and in-row element offset from per-thread
+                // bases (epi_addr.cuh), or the generic forms
+                uint32_t kq, er;
+                if constexpr (kKqK != 0) kq = kq_base[bi][kKqK == 1 ? jv : 0] + epi::addr_delta<KqOff, kE2W0, kKqK>(bi, c, jv);
+                else kq = KqOff::f((int)warp, (int)lane, bi, c, jv);
+                if constexpr (kErK != 0) er = er_base[bi][kErK == 1 ? jv : 0] + epi::addr_delta<ErOff, kE2W0, kErK>(bi, c, jv);
+                else er = ErOff::f((int)warp, (int)lane, bi, c, jv);
                 uint32_t v[2];
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
@@ -793,10 +975,8 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
                 const uint32_t a0 = __shfl_sync(0xffffffffu, v[0], s0), b0 = __shfl_sync(0xffffffffu, v[1], s0);
                 const uint32_t a1 = __shfl_sync(0xffffffffu, v[0], s1), b1 = __shfl_sync(0xffffffffu, v[1], s1);
                 const bool first_row = l4 < 2u;
-                const int lb = 2;
-                const long long o = (((img * C::N + k) >> lb) * p.rows + r0 + sl + (first_row ? 0 : 1)) * 4 +
-                                    2 * (int)(l4 & 1u);
-                *reinterpret_cast<uint2*>(reinterpret_cast<uint32_t*>(p.out) + o) =
+                // ((img N + k) >> 2) rows 4 + (r0 + sl + row) 4 + 2 (l4 & 1), N a multiple of 4
+                *reinterpret_cast<uint2*>(blk_out + (kq * rows4 + er)) =
                     make_uint2(first_row ? a0 : b0, first_row ? a1 : b1);
               }
               continue;
