@@ -724,7 +724,48 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
         const uint32_t cols = (C::M1 == 64) ? 0u : (uint32_t)(buf * C::N1);
         return tmem + (lanes << 16) + cols + (uint32_t)(ch0 + c) * 64u;
       };
-      if constexpr (kIn != kInPairPlanar) {
+      // Overlapped TMEM loads (the next 32-column piece loads while this one is
+      // processed) measured faster for the 2-D convolution's passes and
+      // slower for the C2C transform (half2 N = 256, 512: 4-9 %), which keeps
+      // whole-chunk loads written out in place.
+      if constexpr (kIn == kInNatural) {
+#pragma unroll
+        for (int bi = 0; bi < BPW; ++bi) {
+          const int block = (C::M1 == 64) ? (int)q : (int)(2 * q) + h * BPW + bi;
+          const int rp = block * 8 + (int)(lane >> 2);
+          const int g1 = rp / C::NS, ks = rp % C::NS;
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+            uint32_t r[32];
+            tmem_ld_16x256b_x8(acc1(bi, c), r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int o = 0; o < 8; ++o) {
+              const int pidx = 4 * ((ch0 + c) * 8 + o) + l;
+              const int c1 = pidx / C::NA, a = pidx % C::NA;
+              // a = l + 4*((ch0+c)*8 + o) mod NA -> slot ((ch0+c)*8 + o) mod NA/4
+              // = (c*8 + o) mod NA/4 because ch0*8 is a multiple of NA/4
+              const int slot = (c * 8 + o) % kTw;
+              const float rr = __uint_as_float(r[4 * o]), ri = __uint_as_float(r[4 * o + 1]);
+              const float ir = __uint_as_float(r[4 * o + 2]), ii = __uint_as_float(r[4 * o + 3]);
+              const float yr = rr - ii, yi = ir + ri;
+              const float2 w = tw[bi][slot];
+              const float zr = yr * w.x - yi * w.y, zi = yr * w.y + yi * w.x;
+              uint32_t off;
+              if constexpr (kAK != 0) {
+                off = abase[bi][kAK == 1 ? o : 0] + epi::addr_delta<E1Off, 2, kAK>(bi, c, o);
+              } else {
+                const int sig = g1 * C::C1 + c1;
+                const int g2 = sig / C::C2, c2 = sig % C::C2;
+                const uint32_t krow = (uint32_t)detail::stage2_krow(detail::stage2_rotation(C::kIsHalf, C::kVariant), g2 * C::NA + a);
+                const int col = c2 * 2 * C::NS + 2 * (kColPairs ? detail::stage2_col_pair(ks) : ks);
+                off = (col / C::E) * C::LBO2 + D::swz(krow * 128u + (col % C::E) * C::ESZ);
+              }
+              detail::store_complex<C::kIsHalf>(yb + off, zr, zi);
+            }
+          }
+        }
+      } else if constexpr (kIn != kInPairPlanar) {
         // 32-column pieces, the next one loading while this one is processed
         constexpr int NIT = BPW * CH * 2;
         uint32_t rb[2][16];
@@ -742,6 +783,35 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
             emit1(bi, c, 4 * hh + oo, __uint_as_float(rb[it & 1][4 * oo]), __uint_as_float(rb[it & 1][4 * oo + 1]),
                   __uint_as_float(rb[it & 1][4 * oo + 2]), __uint_as_float(rb[it & 1][4 * oo + 3]));
         }
+      } else if constexpr (kIn == kInPairPlanar && GC == 1 && C::NA == 32) {
+        // pair-planar, NA = 32: output o of a chunk needs column groups jr and
+        // jr + 4 (re and im planes, jr = o / 2).  Pieces of 16 registers hold
+        // groups {2p, 2p+1, 2p+4, 2p+5} (two 16-column loads); the next piece
+        // loads while this one is processed.
+        constexpr int NIT = BPW * CH * 2;
+        uint32_t rb[2][16];
+        auto piece = [&](int it, uint32_t (&v)[16]) {
+          const uint32_t a = acc1(it / (2 * CH), (it / 2) % CH) + 16u * (uint32_t)(it & 1);
+          tmem_ld_16x256b_x2(a, *reinterpret_cast<uint32_t(*)[8]>(&v[0]));
+          tmem_ld_16x256b_x2(a + 32u, *reinterpret_cast<uint32_t(*)[8]>(&v[8]));
+        };
+        piece(0, rb[0]);
+#pragma unroll
+        for (int it = 0; it < NIT; ++it) {
+          tmem_wait_ld();
+          tmem_regs_ready(rb[it & 1]);
+          if (it + 1 < NIT) piece(it + 1, rb[(it + 1) & 1]);
+          const int bi = it / (2 * CH), c = (it / 2) % CH, pc = it & 1;
+#pragma unroll
+          for (int jq = 0; jq < 2; ++jq) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int o = 2 * (2 * pc + jq) + e;
+              emit1(bi, c, o, __uint_as_float(rb[it & 1][4 * jq + e]), __uint_as_float(rb[it & 1][8 + 4 * jq + e]),
+                    __uint_as_float(rb[it & 1][4 * jq + 2 + e]), __uint_as_float(rb[it & 1][8 + 4 * jq + 2 + e]));
+            }
+          }
+        }
       } else {
 #pragma unroll
         for (int bi = 0; bi < BPW; ++bi) {
@@ -754,10 +824,13 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
 #pragma unroll
             for (int o = 0; o < 8 * GC; ++o) {
               // registers of cos*re, cos*im, sin*re, sin*im of this output
-              constexpr int d = C::NA / 8;  // sub-chunks between the re and im planes
-              const int jr = (C::NA == 16) ? ((o >> 1) >> 1) * 4 + ((o >> 1) & 1) : (o >> 1);
-              const int e = o & 1;
-              const int iRR = 4 * jr + e, iIR = 4 * jr + 2 + e, iRI = 4 * (jr + d) + e, iII = 4 * (jr + d) + 2 + e;
+              int iRR = 4 * o, iRI = 4 * o + 1, iIR = 4 * o + 2, iII = 4 * o + 3;
+              if constexpr (kIn == kInPairPlanar) {
+                constexpr int d = C::NA / 8;  // sub-chunks between the re and im planes
+                const int jr = (C::NA == 16) ? ((o >> 1) >> 1) * 4 + ((o >> 1) & 1) : (o >> 1);
+                const int e = o & 1;
+                iRR = 4 * jr + e; iIR = 4 * jr + 2 + e; iRI = 4 * (jr + d) + e; iII = 4 * (jr + d) + 2 + e;
+              }
               emit1(bi, c, o, __uint_as_float(r[iRR >> 5][iRR & 31]), __uint_as_float(r[iRI >> 5][iRI & 31]),
                     __uint_as_float(r[iIR >> 5][iIR & 31]), __uint_as_float(r[iII >> 5][iII & 31]));
             }
@@ -862,21 +935,37 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
           // and k0 + 1 of one signal (stage2_col_pair)
           constexpr int kVec = kOutHalf ? 8 : 16;   // bytes of two complex outputs
           const bool vec_ok = kEpi != kEpiNatural || (reinterpret_cast<uintptr_t>(p.out) & (kVec - 1)) == 0;
-          // 32-column pieces, the next one loading while this one is processed
-          constexpr int NIT2 = CH * 2;
+          // 32-column pieces.  The 2-D convolution's passes load the next piece
+          // while this one is processed (faster there); the C2C transform loads
+          // whole 64-column chunks (the overlapped form measured 4-9 % slower
+          // for half2 N = 256 and 512).
+          constexpr bool kOverlap2 = !(kEpi == kEpiNatural && kIn == kInNatural);
+          constexpr int NIT2 = kOverlap2 ? CH * 2 : CH;
           uint32_t rb[2][16];
-          tmem_ld_16x256b_x4(tmem + (lanes << 16) + cols + (uint32_t)ch0 * 64u, rb[0]);
+          if constexpr (kOverlap2) tmem_ld_16x256b_x4(tmem + (lanes << 16) + cols + (uint32_t)ch0 * 64u, rb[0]);
 #pragma unroll
           for (int it = 0; it < NIT2; ++it) {
-            tmem_wait_ld();
-            tmem_regs_ready(rb[it & 1]);
-            if (it + 1 < NIT2)
-              tmem_ld_16x256b_x4(tmem + (lanes << 16) + cols + (uint32_t)(ch0 + (it + 1) / 2) * 64u + 32u * (uint32_t)((it + 1) & 1),
-                                 rb[(it + 1) & 1]);
-            const int c = it / 2;
-            const uint32_t (&r)[16] = rb[it & 1];
+            uint32_t rw[32];
+            const uint32_t* r;
+            int c, jlo;
+            if constexpr (kOverlap2) {
+              tmem_wait_ld();
+              tmem_regs_ready(rb[it & 1]);
+              if (it + 1 < NIT2)
+                tmem_ld_16x256b_x4(tmem + (lanes << 16) + cols + (uint32_t)(ch0 + (it + 1) / 2) * 64u + 32u * (uint32_t)((it + 1) & 1),
+                                   rb[(it + 1) & 1]);
+              r = rb[it & 1];
+              c = it / 2;
+              jlo = 4 * (it & 1);
+            } else {
+              tmem_ld_16x256b_x8(tmem + (lanes << 16) + cols + (uint32_t)(ch0 + it) * 64u, rw);
+              tmem_wait_ld();
+              r = rw;
+              c = it;
+              jlo = 0;
+            }
 #pragma unroll
-            for (int j = 4 * (it & 1); j < 4 * (it & 1) + 4; j += 2) {
+            for (int j = jlo; j < jlo + (kOverlap2 ? 4 : 8); j += 2) {
               // element offset sl * N + k0 and signal sl from per-thread bases
               // (epi_addr.cuh; the generic forms otherwise)
               uint32_t pos, sl_u, sbyte = 0u;
@@ -892,9 +981,9 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
               float xr[2], xi[2];
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
-                const int jl = (j + e) & 3;   // register group within the 32-column piece
-                const float rr = __uint_as_float(r[4 * jl + 0]), ri = __uint_as_float(r[4 * jl + 1]);
-                const float ir = __uint_as_float(r[4 * jl + 2]), ii = __uint_as_float(r[4 * jl + 3]);
+                const int jj = kOverlap2 ? (j + e) & 3 : j + e;   // register group in r
+                const float rr = __uint_as_float(r[4 * jj + 0]), ri = __uint_as_float(r[4 * jj + 1]);
+                const float ir = __uint_as_float(r[4 * jj + 2]), ii = __uint_as_float(r[4 * jj + 3]);
                 xr[e] = rr - ii;
                 xi[e] = ir + ri;
               }
@@ -941,6 +1030,59 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
         const bool pair_rows = kPairRows && p.blk_log2 == 2;
         // tile base of the paired-row blocked output: img N rows + r0 * 4 elements
         uint32_t* const blk_out = reinterpret_cast<uint32_t*>(p.out) + (img * C::N * p.rows + r0 * 4);
+        if constexpr (kPairRows && (C::NS == 16 || C::NS == 8)) {
+          if (pair_rows) {
+            // Stored iteration j pairs with j + PJ (PJ = NS / 4).  Pieces of 16
+            // registers hold column groups {j0, j0 + 1, j0 + PJ, j0 + PJ + 1}
+            // (two 16-column loads), the next piece loading while this one is
+            // processed.
+            constexpr int PJ = C::NS / 4;
+            const uint32_t l4 = lane & 3u, qbase = lane & ~3u;
+            const uint32_t s0 = qbase + ((2u * l4) & 3u), s1 = qbase + ((2u * l4 + 1u) & 3u);
+            const bool first_row = l4 < 2u;
+            constexpr int NIT = CH * 2;
+            // first stored iteration of piece it: PJ = 4 -> 2 (it & 1); PJ = 2 -> 4 (it & 1)
+            auto j0_of = [](int it) { return (PJ == 4 ? 2 : 4) * (it & 1); };
+            auto piece = [&](int it, uint32_t (&v)[16]) {
+              const uint32_t a = tmem + (lanes << 16) + cols + (uint32_t)(ch0 + it / 2) * 64u + 8u * (uint32_t)j0_of(it);
+              tmem_ld_16x256b_x2(a, *reinterpret_cast<uint32_t(*)[8]>(&v[0]));
+              tmem_ld_16x256b_x2(a + 8u * PJ, *reinterpret_cast<uint32_t(*)[8]>(&v[8]));
+            };
+            uint32_t rb[2][16];
+            piece(0, rb[0]);
+#pragma unroll
+            for (int it = 0; it < NIT; ++it) {
+              tmem_wait_ld();
+              tmem_regs_ready(rb[it & 1]);
+              if (it + 1 < NIT) piece(it + 1, rb[(it + 1) & 1]);
+              const int c = it / 2;
+#pragma unroll
+              for (int jq = 0; jq < 2; ++jq) {
+                const int j = j0_of(it) + jq;
+                const int jv = (j / (2 * PJ)) * PJ + j % PJ;
+                uint32_t kq, er;
+                if constexpr (kKqK != 0) kq = kq_base[bi][kKqK == 1 ? jv : 0] + epi::addr_delta<KqOff, kE2W0, kKqK>(bi, c, jv);
+                else kq = KqOff::f((int)warp, (int)lane, bi, c, jv);
+                if constexpr (kErK != 0) er = er_base[bi][kErK == 1 ? jv : 0] + epi::addr_delta<ErOff, kE2W0, kErK>(bi, c, jv);
+                else er = ErOff::f((int)warp, (int)lane, bi, c, jv);
+                uint32_t v[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const uint32_t* g = &rb[it & 1][8 * e + 4 * jq];   // group j (e = 0) or j + PJ (e = 1)
+                  const float rr = __uint_as_float(g[0]), ri = __uint_as_float(g[1]);
+                  const float ir = __uint_as_float(g[2]), ii = __uint_as_float(g[3]);
+                  __half2 hh = __floats2half2_rn((rr - ii) * osc, (ir + ri) * osc);
+                  v[e] = *reinterpret_cast<uint32_t*>(&hh);
+                }
+                const uint32_t a0 = __shfl_sync(0xffffffffu, v[0], s0), b0 = __shfl_sync(0xffffffffu, v[1], s0);
+                const uint32_t a1 = __shfl_sync(0xffffffffu, v[0], s1), b1 = __shfl_sync(0xffffffffu, v[1], s1);
+                *reinterpret_cast<uint2*>(blk_out + (kq * rows4 + er)) =
+                    make_uint2(first_row ? a0 : b0, first_row ? a1 : b1);
+              }
+            }
+            continue;
+          }
+        }
 #pragma unroll
         for (int c = 0; c < CH; ++c) {
           uint32_t r[32];
