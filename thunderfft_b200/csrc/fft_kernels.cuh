@@ -156,7 +156,16 @@ struct Fft2Cfg {
   static_assert(SMEM_BYTES + 512 <= 232448, "shared memory budget");
   static constexpr int EPW = S::EPW;                       // epilogue warps per TMEM lane quadrant
   static constexpr int kEpiWarps = 4 * EPW;                // per epilogue stage
-  static constexpr int kThreads = 32 * (2 + 2 * kEpiWarps); // producer, MMA, 2 x 8 epilogue warps
+  // Warps: producer, MMA issuer, the two epilogue groups, and (kSplitMma) a
+  // second MMA issuer for stage 2.  One thread issuing both stages' MMAs
+  // waits on each stage's barriers in turn while its tcgen05.mma issue stalls
+  // for most of the previous stage's execution (a clock64 timeline of half2
+  // N = 4096 showed the issuing thread busy ~1400 of ~1750 cycles per tile).
+  // Measured per storage type: half2 C2C gained 1-10 % (N = 4096: 0.74 ->
+  // 0.81 of the copy peak), float2 lost 1-2 %, so float2 keeps one issuer.
+  static constexpr bool kSplitMma = kHalf;
+  static constexpr int kMma2Warp = kSplitMma ? 2 + 2 * kEpiWarps : -1;
+  static constexpr int kThreads = 32 * (2 + 2 * kEpiWarps + (kSplitMma ? 1 : 0));
 };
 
 // Host-visible kernel parameters (besides tensor maps).
@@ -428,7 +437,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN];
   __shared__ uint64_t bar_acc1_full[2], bar_acc1_empty[2], bar_y_full[2], bar_y_empty[2];
-  __shared__ uint64_t bar_acc2_full[2], bar_acc2_empty[2], bar_const, bar_done;
+  __shared__ uint64_t bar_acc2_full[2], bar_acc2_empty[2], bar_const, bar_done, bar_done2;
   __shared__ uint64_t bar_h_full[C::HS > 0 ? C::HS : 1], bar_h_empty[C::HS > 0 ? C::HS : 1];
   __shared__ uint32_t tmem_slot;
   constexpr bool kStageH = kEpi == kEpiMulNatural && C::HS > 0;   // spectrum tiles via TMA
@@ -449,6 +458,7 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
     }
     mbar_init(&bar_const, 1);
     mbar_init(&bar_done, 1);
+    mbar_init(&bar_done2, 1);
     if constexpr (kStageH)
       for (int i = 0; i < C::HS; ++i) { mbar_init(&bar_h_full[i], 1); mbar_init(&bar_h_empty[i], C::kEpiWarps); }
     fence_mbar_init();
@@ -458,6 +468,34 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+
+  // Stage-2 MMAs of tile j, issued by one thread (the MMA issuer, or the
+  // second issuer with kSplitMma); false when a wait gave up.
+  auto issue_stage2 = [&](int j) -> bool {
+    using namespace sm100;
+    const int buf = j & 1;
+    const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+    if (!mbar_wait(&bar_y_full[buf], ph, p.err, kDevTimeoutMma)) return false;
+    if (!mbar_wait(&bar_acc2_empty[buf], ph ^ 1u, p.err, kDevTimeoutMma)) return false;
+    tc_fence_after();
+    const uint32_t idesc2 = instr_desc(D::kFmt, C::M2, C::N2, 0, 1);
+    const uint32_t lboA2 = (C::M2 / 8) * 128;   // A image: K-major, no swizzle
+    const uint64_t adA2 = smem_desc(smem_u32(smem + C::OFF_A2), lboA2, 128, kSwNone);
+    const uint64_t bd0 = smem_desc(smem_u32(smem + C::OFF_Y), C::LBO2, D::kBSbo, D::kBSwizzle) +
+                         (uint64_t)(buf * (C::TILE_BYTES >> 4));
+    const uint32_t d = (C::M2 == 64) ? tmem + 256u + ((uint32_t)(16 * buf) << 16)
+                                     : tmem + 256u + (uint32_t)(buf * C::N2);
+#pragma unroll
+    for (int k = 0; k < C::KSTEPS2; ++k) {
+      const uint64_t ad = adA2 + (uint64_t)((k * 2 * lboA2) >> 4);
+      const uint64_t bd = bd0 + (uint64_t)((k * C::KSTEP_BYTES) >> 4);
+      if constexpr (C::kIsHalf) umma_f16(d, ad, bd, idesc2, k > 0);
+      else umma_tf32(d, ad, bd, idesc2, k > 0);
+    }
+    umma_commit(&bar_y_empty[buf]);
+    umma_commit(&bar_acc2_full[buf]);
+    return true;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -564,19 +602,18 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait(&bar_const, 0, p.err, kDevTimeoutMma);
-      const uint32_t a1 = smem_u32(smem + C::OFF_A1), a2 = smem_u32(smem + C::OFF_A2);
+      const uint32_t a1 = smem_u32(smem + C::OFF_A1);
       const uint32_t idesc1 = instr_desc(D::kFmt, C::M1, C::N1, 0, 1);
-      const uint32_t idesc2 = instr_desc(D::kFmt, C::M2, C::N2, 0, 1);
       // A images: K-major, no swizzle, core matrix (8 rows x 16 B) contiguous;
       // LBO = K-direction core stride = M/8 * 128 B, SBO = 128 B.
-      const uint32_t lboA1 = (C::M1 / 8) * 128, lboA2 = (C::M2 / 8) * 128;
+      const uint32_t lboA1 = (C::M1 / 8) * 128;
       // Descriptors are built once; a K step, an input slot or a Y buffer adds
       // its byte offset >> 4 to the start-address field (shared addresses
       // < 256 KB never carry out of it).  The issuing thread then spends a
       // few integer adds per MMA.
-      const uint64_t adA1 = smem_desc(a1, lboA1, 128, kSwNone), adA2 = smem_desc(a2, lboA2, 128, kSwNone);
+      const uint64_t adA1 = smem_desc(a1, lboA1, 128, kSwNone);
       const uint64_t bdIn0 = smem_desc(smem_u32(smem + C::OFF_IN), C::LBO1, D::kBSbo, D::kBSwizzle);
-      const uint64_t bdY0 = smem_desc(smem_u32(smem + C::OFF_Y), C::LBO2, D::kBSbo, D::kBSwizzle);
+      // stage 1 of tile i, then (one issuer) stage 2 of tile i - 1
       for (int i = 0; ok && i <= my_tiles; ++i) {
         if (i < my_tiles) {
           const int slot = i % C::SIN, buf = i & 1;
@@ -595,29 +632,23 @@ fft2_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_constant__
           umma_commit(&bar_in_empty[slot]);
           umma_commit(&bar_acc1_full[buf]);
         }
-        if (i > 0) {
-          const int j = i - 1, buf = j & 1;
-          const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-          if (!mbar_wait(&bar_y_full[buf], ph, p.err, kDevTimeoutMma)) { ok = false; break; }
-          if (!mbar_wait(&bar_acc2_empty[buf], ph ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t bd0 = bdY0 + (uint64_t)(buf * (C::TILE_BYTES >> 4));
-          const uint32_t d = (C::M2 == 64) ? tmem + 256u + ((uint32_t)(16 * buf) << 16)
-                                           : tmem + 256u + (uint32_t)(buf * C::N2);
-#pragma unroll
-          for (int k = 0; k < C::KSTEPS2; ++k) {
-            const uint64_t ad = adA2 + (uint64_t)((k * 2 * lboA2) >> 4);
-            const uint64_t bd = bd0 + (uint64_t)((k * C::KSTEP_BYTES) >> 4);
-            if constexpr (C::kIsHalf) umma_f16(d, ad, bd, idesc2, k > 0);
-            else umma_tf32(d, ad, bd, idesc2, k > 0);
-          }
-          umma_commit(&bar_y_empty[buf]);
-          umma_commit(&bar_acc2_full[buf]);
+        if constexpr (!C::kSplitMma) {
+          if (i > 0 && !issue_stage2(i - 1)) { ok = false; break; }
         }
       }
       // drain: all issued MMAs complete before TMEM is released
       umma_commit(&bar_done);
       mbar_wait(&bar_done, 0, p.err, kDevTimeoutMma);
+    }
+    __syncwarp();
+  } else if (C::kSplitMma && warp == (uint32_t)C::kMma2Warp) {
+    // ------------------------------------------------------------ stage-2 MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar_const, 0, p.err, kDevTimeoutMma);
+      for (int j = 0; ok && j < my_tiles; ++j)
+        if (!issue_stage2(j)) ok = false;
+      umma_commit(&bar_done2);
+      mbar_wait(&bar_done2, 0, p.err, kDevTimeoutMma);
     }
     __syncwarp();
   } else if (warp < 2 + C::kEpiWarps) {
