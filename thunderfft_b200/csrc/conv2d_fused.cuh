@@ -97,7 +97,11 @@ struct Conv2dColCfg {
   // twiddles spill under the 96-register cap of 576 threads.
   static constexpr int EPW = (kHalf || kN <= 512) ? 2 : 1;
   static constexpr int kEpiWarps = 4 * EPW;                   // per epilogue group
-  static constexpr int kThreads = 32 * (2 + 2 * kEpiWarps);
+  // Two MMA issuers: warp 1 issues stages 1 and 3, warp kMma2Warp (after the
+  // epilogue warps) stages 2 and 4, so a wait or a stalled issue of one
+  // stage does not hold up the others.
+  static constexpr int kMma2Warp = 2 + 2 * kEpiWarps;
+  static constexpr int kThreads = 32 * (kMma2Warp + 1);
   // TMEM accumulators: D1/D4 in columns [0, 256), D2/D3 in [256, 512); an
   // M = 64 pair shares its columns through lanes 0-15 / 16-31 of each
   // quadrant, an M = 128 pair splits the columns.
@@ -648,7 +652,7 @@ conv2d_cols_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_con
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t bar_in_full[C::SIN], bar_in_empty[C::SIN], bar_h_full[C::HS], bar_h_empty[C::HS];
-  __shared__ uint64_t bar_d_full[4], bar_d_empty[4], bar_b_full[3], bar_b_empty[3], bar_const, bar_done;
+  __shared__ uint64_t bar_d_full[4], bar_d_empty[4], bar_b_full[3], bar_b_empty[3], bar_const, bar_done[2];
   __shared__ uint32_t tmem_slot;
 
   const uint32_t warp = warp_id(), lane = lane_id();
@@ -662,7 +666,8 @@ conv2d_cols_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_con
     for (int i = 0; i < 4; ++i) { mbar_init(&bar_d_full[i], 1); mbar_init(&bar_d_empty[i], C::kEpiWarps); }
     for (int i = 0; i < 3; ++i) { mbar_init(&bar_b_full[i], C::kEpiWarps); mbar_init(&bar_b_empty[i], 1); }
     mbar_init(&bar_const, 1);
-    mbar_init(&bar_done, 1);
+    mbar_init(&bar_done[0], 1);
+    mbar_init(&bar_done[1], 1);
     fence_mbar_init();
   }
   if (warp == 1) { tmem_alloc(&tmem_slot, 512); tmem_relinquish(); }
@@ -703,8 +708,10 @@ conv2d_cols_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_con
       }
       __syncwarp();
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == (uint32_t)C::kMma2Warp) {
+    // ------------------------------------------------------------ MMA issuers
+    // warp 1: stages 1 and 3; warp kMma2Warp: stages 2 and 4
+    const int par = (warp == 1) ? 0 : 1;
     if (lane == 0) {
       bool ok = mbar_wait(&bar_const, 0, p.err, kDevTimeoutMma);
       const uint32_t idesc1 = instr_desc(D::kFmt, C::M1, C::N1, 0, 1);
@@ -732,7 +739,7 @@ conv2d_cols_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_con
         }
       };
       for (int r = 0; ok && r < ntiles + 3; ++r) {
-        if (r < ntiles) {   // S1(r): input slot -> D1
+        if (par == 0 && r < ntiles) {   // S1(r): input slot -> D1
           const int slot = r % C::SIN;
           if (!mbar_wait(&bar_in_full[slot], (uint32_t)(r / C::SIN) & 1u, p.err, kDevTimeoutMma) ||
               !mbar_wait(&bar_d_empty[0], ((uint32_t)r & 1u) ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
@@ -744,7 +751,7 @@ conv2d_cols_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_con
 #pragma unroll 1
         for (int s = 1; s < 4; ++s) {   // S2(r-1), S3(r-2), S4(r-3): B(s+1) -> D(s+1)
           const int j = r - s;
-          if (j < 0 || j >= ntiles) continue;
+          if ((s & 1) != (par ^ 1) || j < 0 || j >= ntiles) continue;
           if (!mbar_wait(&bar_b_full[s - 1], (uint32_t)j & 1u, p.err, kDevTimeoutMma) ||
               !mbar_wait(&bar_d_empty[s], ((uint32_t)j & 1u) ^ 1u, p.err, kDevTimeoutMma)) { ok = false; break; }
           tc_fence_after();
@@ -756,8 +763,8 @@ conv2d_cols_kernel(const __grid_constant__ CUtensorMap tmap_in, const __grid_con
         }
       }
       // drain: all issued MMAs complete before TMEM is released
-      umma_commit(&bar_done);
-      mbar_wait(&bar_done, 0, p.err, kDevTimeoutMma);
+      umma_commit(&bar_done[par]);
+      mbar_wait(&bar_done[par], 0, p.err, kDevTimeoutMma);
     }
     __syncwarp();
   } else {
