@@ -29,9 +29,10 @@
 // of both in one half2 and the imaginary parts in another, so each half2
 // instruction advances two butterflies with the same twiddles.  A pass with
 // a single butterfly per thread (the radix-32 passes of N >= 1024) runs in
-// FP32 between half2 loads and stores.  half2 N = 64 (16 signals) and
-// N = 128 (8 signals) instead run two warp-MMA DFT stages on their own
-// fragment orders (thunderfft_impl_device_mma.cuh).
+// FP32 between half2 loads and stores.  half2 N = 64 (16 signals) instead
+// runs two warp-MMA DFT stages, and N = 128 (8 signals) the float2 TF32
+// warp-MMA routine on FP32 copies of its registers, each on its own fragment
+// orders (thunderfft_impl_device_mma.cuh).
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -493,8 +494,16 @@ __device__ __forceinline__ void ThunderFFT_kernel_reg(vec2_t<T>* __restrict__ re
   vec2_t<T>* ws = static_cast<vec2_t<T>*>(workspace);
   const int t = detail::block_thread();
   if constexpr (detail::mfft::enabled<T, N, batch>) {
-    if constexpr (N == 64) detail::mfft::run64<T, forward>(reg, ws, t);
-    else detail::mfft::run128<forward>(reg, ws, t);
+    detail::mfft::run64<T, forward>(reg, ws, t);
+  } else if constexpr (detail::mfft::tf32_enabled<T, N, batch> && std::is_same_v<T, half>) {
+    // half2 N = 128: the TF32 routine on FP32 copies of the registers (the
+    // half2 values are exact in TF32; FP32 accumulation), rounded back
+    float2 r[detail::frag<N, batch>::EPT];
+#pragma unroll
+    for (int i = 0; i < detail::frag<N, batch>::EPT; ++i) r[i] = __half22float2(reg[i]);
+    detail::mfft::run128_tf32<forward>(r, t);
+#pragma unroll
+    for (int i = 0; i < detail::frag<N, batch>::EPT; ++i) reg[i] = __float22half2_rn(r[i]);
   } else if constexpr (detail::mfft::tf32_enabled<T, N, batch>) {
     float2* r = reinterpret_cast<float2*>(reg);
     if constexpr (N == 64) detail::mfft::run64_tf32<forward>(r, t);

@@ -2,10 +2,12 @@
 // (the reference computes its device routine with warp MMAs too:
 // detail/kernel/unit_kernel_fp32.cuh, unit_kernel_fp16.cuh), each written for
 // this library's own operand maps:
-//   * half2 N = 64 (16 signals, one warp) as two FP16 MMA DFT stages, and
-//     N = 128 on top of it (run64, run128);
+//   * half2 N = 64 (16 signals, one warp) as two FP16 MMA DFT stages (run64);
 //   * float2 N = 64, 128, 256 with one TF32 MMA stage (radix 4, 8, 4) and
-//     in-lane FP32 DFTs (run64_tf32, run128_tf32, run256_tf32, at the end).
+//     in-lane FP32 DFTs (run64_tf32, run128_tf32, run256_tf32, at the end);
+//     half2 N = 128 runs run128_tf32 on FP32 copies of its registers (half2
+//     values are exact in TF32): 1.56 us per paper-benchmark call against
+//     1.97 us for a radix-2 step on top of run64, at rel-L2 2.4e-4.
 // The run64 template's float2 branches are not used (run64_tf32 serves
 // float2 N = 64).
 //
@@ -55,11 +57,9 @@ namespace mfft {
 // signals per block: 0.49 us per paper-benchmark call (16384 signals) against
 // 1.02 us for the packed-FP16 register FFT.  Its float2 form (mma.m16n8k8
 // .tf32, 64 MMAs and a shared-memory exchange per call) measured 1.24 us;
-// run64_tf32 (16 MMAs, no exchange) takes 0.48 us.  half2 N = 128 (8
-// signals) reuses it on 16 rows after a radix-2 step (run128).
+// run64_tf32 (16 MMAs, no exchange) takes 0.48 us.
 template <typename T, int N, int batch>
-inline constexpr bool enabled =
-    std::is_same_v<T, half> && ((N == 64 && batch == 16) || (N == 128 && batch == 8));
+inline constexpr bool enabled = std::is_same_v<T, half> && N == 64 && batch == 16;
 
 // Fragment slot i of block thread t: signal j, element n (the order above).
 __device__ __forceinline__ void frag64(int t, int i, int& j, int& n) {
@@ -257,16 +257,6 @@ __device__ __forceinline__ void run64(vec2_t<T>* reg, vec2_t<T>* ws, int t) {
   }
 }
 
-// half2 N = 128, 8 signals per warp (frag128).  A radix-2 decimation-in-
-// frequency step in registers,
-//   a[n] = x[n] + x[n + 64],  b[n] = (x[n] - x[n + 64]) w_128^n   (n < 64),
-// turns the lane's two chunks of signal gid into rows gid (a) and gid + 8 (b)
-// of the 64-point routine, whose outputs are A[k] = X[2k] and B[k] =
-// X[2k + 1].  One shared-memory pass then puts X back in frag128 order, so
-// the output order equals the input order.
-constexpr int kEx128Sig = 136;   // 8 * 136 = (128 + pad_h(128)) * 8
-__host__ __device__ constexpr int ex128_pos(int k) { return k ^ (((k >> 5) & 1) << 2); }
-
 // (cos, sin)(2 pi i / 128) for i < 16, as compile-time constants
 // (sin(x) = cos(pi/2 - x) with a short Taylor series in double).
 __host__ __device__ constexpr double taylor_cos(double x) {
@@ -282,54 +272,6 @@ struct Root128 {
   static constexpr double x = 6.283185307179586476925 * I / 128.0;
   static constexpr float c = float(taylor_cos(x)), s = float(taylor_cos(1.5707963267948966192 - x));
 };
-
-template <bool fwd, int... I>
-__device__ __forceinline__ void radix2_dif128(half2* reg, float2 wt, std::integer_sequence<int, I...>) {
-  // twiddle w_128^(16 tig + i) = w_8^tig * w_128^i: one per-lane root times a
-  // compile-time constant; applied as a packed complex multiply,
-  // (dr, di) * (wr, wi) = (dr, di) * (wr, wr) + (di, dr) * (-wi, wi)
-  (
-      [&] {
-        constexpr float ci = Root128<I>::c, si = fwd ? -Root128<I>::s : Root128<I>::s;
-        const float wr = wt.x * ci - wt.y * si, wi = wt.x * si + wt.y * ci;
-        const half2 wrr = __floats2half2_rn(wr, wr), wii = __floats2half2_rn(-wi, wi);
-        const half2 x0 = reg[I], x1 = reg[16 + I];
-        const half2 d = __hsub2(x0, x1);
-        reg[I] = __hadd2(x0, x1);
-        reg[16 + I] = __hfma2(__lowhigh2highlow(d), wii, __hmul2(d, wrr));
-      }(),
-      ...);
-}
-
-template <bool fwd>
-__device__ __forceinline__ void run128(half2* reg, half2* ws, int t) {
-  const int lane = t & 31, gid = lane >> 2, tig = lane & 3;
-  {
-    const float2 w8 = unit_root(16 * tig, 128);
-    radix2_dif128<fwd>(reg, make_float2(w8.x, fwd ? -w8.y : w8.y), std::make_integer_sequence<int, 16>{});
-  }
-  run64<half, fwd>(reg, ws, t);
-  // reg[i] = X[2k'], reg[16 + i] = X[2k' + 1], k' = 16 tig + i -> frag128
-  __syncwarp();
-  half2* row = ws + gid * kEx128Sig;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int k = 2 * (16 * tig + i);
-    *reinterpret_cast<uint2*>(row + ex128_pos(k)) =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&reg[i]), *reinterpret_cast<const uint32_t*>(&reg[16 + i]));
-  }
-  __syncwarp();
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const uint4 q = *reinterpret_cast<const uint4*>(row + ex128_pos(64 * h + 16 * tig + 4 * v));
-      reg[16 * h + 4 * v + 0] = *reinterpret_cast<const half2*>(&q.x);
-      reg[16 * h + 4 * v + 1] = *reinterpret_cast<const half2*>(&q.y);
-      reg[16 * h + 4 * v + 2] = *reinterpret_cast<const half2*>(&q.z);
-      reg[16 * h + 4 * v + 3] = *reinterpret_cast<const half2*>(&q.w);
-    }
-}
 
 // ---------------------------------------------------------------------------
 // float2 N = 64, 16 signals per warp, TF32 warp MMAs (the reference's float
@@ -351,7 +293,8 @@ __device__ __forceinline__ void run128(half2* reg, half2* ws, int t) {
 // way with conjugate roots, unnormalized.
 template <typename T, int N, int batch>
 inline constexpr bool tf32_enabled =
-    std::is_same_v<T, float> && ((N == 64 && batch == 16) || (N == 128 && batch == 8) || (N == 256 && batch == 16));
+    (std::is_same_v<T, float> && ((N == 64 && batch == 16) || (N == 128 && batch == 8) || (N == 256 && batch == 16))) ||
+    (std::is_same_v<T, half> && N == 128 && batch == 8);
 // routines whose output fragment order differs from the input order
 template <typename T, int N, int batch>
 inline constexpr bool split_order = tf32_enabled<T, N, batch>;
