@@ -1213,7 +1213,7 @@ thff_status thff_conv2d_async(int dtype, long long nimg_b, int chans, int h, int
     return fail(THFF_INVALID_ARGUMENT, "conv2d: buffers must be 16-byte aligned");
   const long long per_pair = 2LL * h * w * 8;
   if (workspace_bytes / per_pair < 1)
-    return fail(THFF_INVALID_ARGUMENT, "conv2d: workspace smaller than one image pair (2*h*w*16 bytes)");
+    return fail(THFF_INVALID_ARGUMENT, "conv2d: workspace smaller than one image pair (2*h*w*8 bytes)");
   int dev;
   thff_status s = current_device(&dev);
   if (s != THFF_OK) return s;
