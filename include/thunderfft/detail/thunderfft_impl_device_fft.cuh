@@ -479,6 +479,44 @@ __device__ __forceinline__ void run_passes_h(half2* reg, half2* ws, int t) {
   if constexpr (!last) run_passes_h<N, B, EPT, P, fwd, s + 1, Ns * R>(reg, ws, t);
 }
 
+// half2 N = 256, 16 signals, 128 threads (fragment mfft::frag256_h): thread
+// t = 16 p + q runs signals 2p and 2p + 1 as packed pairs.  256 = 16 x 16:
+//   pass 1  Y[q][k1] = sum_r x[q + 16 r] W16^(r k1), times W256^(q k1)
+//   pass 2  X[k1 + 16 k2] = sum_q Y[q][k1] W16^(q k2), thread q' taking k1 = q'
+// One exchange through the workspace: planes of packed real and imaginary
+// parts, pair p's plane row k1 at p (N + pad_h(N)) + 17 k1 (the odd row
+// stride keeps both the row writes and the column reads free of bank
+// conflicts); the two planes use 2 x 8 x 272 = (N + pad_h(N)) x 16 elements.
+template <bool fwd>
+__device__ __forceinline__ void run256_h(half2* reg, half2* ws, int t) {
+  constexpr int kPair = 256 + 256 / 16, kPlane = 8 * kPair;   // N + pad_h(N) per pair
+  const int p = t >> 4, q = t & 15;
+  HP v[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) v[r] = hpack(reg[r], reg[16 + r]);
+  dft<16, fwd>(v);   // v[brev(k1)] = Y[q][k1] before the twiddle
+  float2 w[16];
+  root_powers<16, 16, fwd>(w, q);   // w[k1] = W256^(q k1)
+  half2* const row = ws + p * kPair + q;
+  __syncthreads();  // every thread's reads of the workspace are done
+#pragma unroll
+  for (int k1 = 0; k1 < 16; ++k1) {
+    const HP y = (k1 == 0) ? v[0] : cmulh(v[brev<16>(k1)], hbroadcast(w[k1]));
+    row[17 * k1] = y.re;
+    row[kPlane + 17 * k1] = y.im;
+  }
+  __syncthreads();
+  const half2* const col = ws + p * kPair + 17 * q;
+#pragma unroll
+  for (int qq = 0; qq < 16; ++qq) v[qq] = HP{col[qq], col[kPlane + qq]};
+  dft<16, fwd>(v);   // v[brev(k2)] = X[q + 16 k2]
+#pragma unroll
+  for (int k2 = 0; k2 < 16; ++k2) {
+    reg[k2] = hlo(v[brev<16>(k2)]);
+    reg[16 + k2] = hhi(v[brev<16>(k2)]);
+  }
+}
+
 }  // namespace dfft
 }  // namespace detail
 
@@ -509,6 +547,8 @@ __device__ __forceinline__ void ThunderFFT_kernel_reg(vec2_t<T>* __restrict__ re
     if constexpr (N == 64) detail::mfft::run64_tf32<forward>(r, t);
     else if constexpr (N == 128) detail::mfft::run128_tf32<forward>(r, t);
     else detail::mfft::run256_tf32<forward>(r, reinterpret_cast<float2*>(ws), t);
+  } else if constexpr (detail::mfft::h256_enabled<T, N, batch>) {
+    detail::dfft::run256_h<forward>(reg, ws, t);
   } else if constexpr (std::is_same_v<T, half>) {
     detail::dfft::run_passes_h<N, batch, F::EPT, F::P, forward, 0, 1>(reg, ws, t);
   } else {

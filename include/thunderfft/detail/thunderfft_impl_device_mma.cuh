@@ -299,6 +299,17 @@ inline constexpr bool tf32_enabled =
 template <typename T, int N, int batch>
 inline constexpr bool split_order = tf32_enabled<T, N, batch>;
 
+// half2 N = 256 (16 signals, 4 warps): two radix-16 passes in packed FP16
+// (dfft::run256_h).  Thread t = 16 p + q holds elements q + 16 i' of
+// signals 2p (registers 0-15) and 2p + 1 (registers 16-31), input and
+// output alike.
+template <typename T, int N, int batch>
+inline constexpr bool h256_enabled = std::is_same_v<T, half> && N == 256 && batch == 16;
+__device__ __forceinline__ void frag256_h(int t, int i, int& j, int& n) {
+  j = 2 * (t >> 4) + (i >> 4);
+  n = (t & 15) + 16 * (i & 15);
+}
+
 __device__ __forceinline__ void frag64_tf32_out(int t, int i, int& j, int& k) {
   const int lane = t & 31;
   j = (lane >> 2) + 8 * (i >> 4);

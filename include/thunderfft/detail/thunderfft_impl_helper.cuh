@@ -45,13 +45,16 @@ __device__ __forceinline__ int block_thread() { return threadIdx.x + threadIdx.y
 // Fragment slot i of block thread t holds element n of signal j of the
 // block's tile: t + P i in signal order, except for half2 N = 64 with 16
 // signals and N = 128 with 8, whose warp-MMA routines keep the MMA operand
-// order (mfft::frag64, mfft::frag128).
+// order (mfft::frag64, mfft::frag128), the float2 TF32 routines, and half2
+// N = 256 with 16 signals (mfft::frag256_h: 16 elements of two signals).
 template <typename T, int N, int batch>
 __device__ __forceinline__ void frag_elem(int t, int i, int& j, int& n) {
   if constexpr (mfft::enabled<T, N, batch> || mfft::tf32_enabled<T, N, batch>) {
     if constexpr (N == 64) mfft::frag64(t, i, j, n);
     else if constexpr (N == 128) mfft::frag128(t, i, j, n);
     else mfft::frag256_tf32_in(t, i, j, n);
+  } else if constexpr (mfft::h256_enabled<T, N, batch>) {
+    mfft::frag256_h(t, i, j, n);
   } else {
     const int e = t + frag<N, batch>::P * i;
     j = e / N;
