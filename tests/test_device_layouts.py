@@ -4,7 +4,9 @@ dfft::run256_h; fragment mfft::frag256_h in thunderfft_impl_device_mma.cuh).
 
 The routine's correctness is tested on the GPU (tests/test_header_api.py and
 the reference's validation matrix); these tests pin the layout facts its
-comments state, so a change to the maps that breaks one fails on CPU:
+comments state, so a change to the maps that breaks one fails on CPU.  The
+warp-MMA routines' fragment orders (mfft::frag64, frag128 and the TF32
+input/output orders) are checked the same way for coverage.  For N = 256:
   * the fragment covers every (signal, element) of the 16-signal tile once;
   * the two-pass split 256 = 16 x 16 reproduces the DFT (float64 restatement
     of the same index arithmetic);
@@ -23,6 +25,34 @@ ROW = 17                    # odd row stride of the exchange
 def frag256_h(t, i):
     """(signal, element) held by fragment register i of block thread t."""
     return 2 * (t >> 4) + (i >> 4), (t & 15) + 16 * (i & 15)
+
+
+# Every other fragment order of the warp-MMA routines, restated from
+# thunderfft_impl_device_mma.cuh: (N, batch, threads, map(t, i) -> (j, n)).
+OTHER_ORDERS = {
+    "frag64 (half2 N=64 in/out, float2 N=64 in)": (64, 16, 32, lambda t, i: (
+        ((t & 31) >> 2) + 8 * (i >> 4), 16 * ((t & 31) & 3) + (i & 15))),
+    "frag64_tf32_out": (64, 16, 32, lambda t, i: (
+        ((t & 31) >> 2) + 8 * (i >> 4), ((t & 31) & 3) + 4 * (i & 15))),
+    "frag128 (N=128 in)": (128, 8, 32, lambda t, i: (
+        (t & 31) >> 2, 16 * ((t & 31) & 3) + (i & 15) + 64 * (i >> 4))),
+    "frag128_tf32_out": (128, 8, 32, lambda t, i: (
+        (t & 31) >> 2, 8 * (i & 15) + 4 * (i >> 4) + ((t & 31) & 3))),
+    "frag256_tf32_in": (256, 16, 128, lambda t, i: (
+        ((t & 31) >> 2) + 8 * (i >> 4), 16 * (t >> 5) + (i & 15) + 64 * ((t & 31) & 3))),
+    "frag256_tf32_out": (256, 16, 128, lambda t, i: (
+        ((t & 31) >> 2) + 8 * (i >> 4), 16 * (i & 15) + 4 * ((t & 31) & 3) + (t >> 5))),
+}
+
+
+def test_other_fragment_orders_cover_tile_once():
+    for name, (n, batch, threads, f) in OTHER_ORDERS.items():
+        seen = np.zeros((batch, n), dtype=np.int64)
+        for t in range(threads):
+            for i in range(n * batch // threads):
+                j, e = f(t, i)
+                seen[j, e] += 1
+        assert (seen == 1).all(), name
 
 
 def test_fragment_covers_tile_once():
