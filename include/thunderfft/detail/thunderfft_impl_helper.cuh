@@ -63,9 +63,10 @@ __device__ __forceinline__ void frag_elem(int t, int i, int& j, int& n) {
 }
 
 // Fragment slot i of block thread t in an OUTPUT fragment: the input order
-// (frag_elem), except for the float2 warp-MMA routines (N = 64, 128, 256),
-// which end with an in-lane DFT and leave its outputs in the lane that
-// computed them (mfft::frag64_tf32_out, frag128_tf32_out, frag256_tf32_out).
+// (frag_elem), except for the TF32 warp-MMA routines (float2 N = 64, 128,
+// 256 and half2 N = 128), which end with an in-lane DFT and leave its
+// outputs in the lane that computed them (mfft::frag64_tf32_out,
+// frag128_tf32_out, frag256_tf32_out).
 template <typename T, int N, int batch>
 __device__ __forceinline__ void frag_elem_out(int t, int i, int& j, int& k) {
   if constexpr (mfft::split_order<T, N, batch>) {
